@@ -1,0 +1,377 @@
+"""Benchmark of the tcaspmm hot path, C = A @ B (CSR A, dense row-major B).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gcn|ffn|sage|skew] [--impl ours|reference]
+
+Default workload: the GCN aggregation config (R-MAT a=0.57 b=0.19 c=0.19, 2^20
+nodes, 30M directed draws, symmetrised + self-loops, values 1/sqrt(d_i d_j),
+X 1M x 128 N(0,1) fp32), seeded synthetic data.  One step = one SpMM over the
+whole matrix.  With N GPUs (torchrun, one rank per GPU) each rank owns a column
+block of B and C (A replicated, no collective on the data path); value = total
+GFLOP/s of the whole job (2 nnz N / max-over-ranks time).
+
+``--impl reference`` times the reference semantics on the host cores instead:
+the reference ships no CPU CSR loop, so this is the fp32 OpenMP CSR loop of
+oracle/oracle.c (a restatement of src/our_spmm.cu's arithmetic), run by rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "SpMM GFLOP/s (2*nnz*N)"
+UNIT = "GFLOP/s"
+L2_BYTES = 126 * 2**20
+
+WORKLOADS = {
+    # name: (description, builder, N, dtype)
+    "gcn": ("C3 GCN aggregation: R-MAT(0.57,0.19,0.19) 2^20 nodes, 30M draws, symmetrised + self-loops, "
+            "1/sqrt(d_i d_j); X 1M x 128 fp32", lambda T: T.gen_rmat(20, 30_000_000, kind="gcn", seed=0), 128, "f32"),
+    "ffn": ("C1 pruned FFN: A 2048x512 70% uniform sparsity, N(0,1); B 512x256 N(0,1) fp16",
+            lambda T: T.gen_uniform(2048, 512, 0.3, 0), 256, "f16"),
+    "sage": ("C4 GraphSAGE mean: R-MAT 2^22 nodes, 100M draws, 1/deg(i); X 4M x 256 fp16",
+             lambda T: T.gen_rmat(22, 100_000_000, kind="sage", seed=0), 256, "f16"),
+    "skew": ("C5 extreme skew: 8M x 8M, 64 hub rows x 200k nnz + Poisson(3) rows, U(-1,1); B 8M x 64 fp16",
+             lambda T: T.gen_skew(1 << 23, 64, 200_000, 3.0, seed=0), 64, "f16"),
+}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic(workload: str):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary, or None."""
+    p = os.path.join(ROOT, "profiles", "traffic.json.txt")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        d = json.load(f)
+    return d.get(workload)
+
+
+class ClockSampler:
+    """Polls NVML (SM clock, throttle reasons) in a thread during the timed region."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, local_rank: int, period_s: float = 0.005):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self.period = period_s
+        self._stop = threading.Event()
+        self._h = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            # NVML numbers GPUs physically; map through CUDA_VISIBLE_DEVICES.
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+            entry = vis.split(",")[local_rank].strip() if vis else str(local_rank)
+            if entry.isdigit():
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(int(entry))
+            else:
+                self._h = pynvml.nvmlDeviceGetHandleByUUID(entry)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # pragma: no cover - reported in the JSON
+            self.error = str(e)
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self._nv.nvmlDeviceGetClockInfo(self._h, self._nv.NVML_CLOCK_SM))
+                mask = self._nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for bit, name in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t.is_alive():
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+
+
+def algorithmic_bytes(M, K, nnz, N, elem):
+    return (M + 1) * 4 + nnz * (4 + elem) + K * N * elem + M * N * 4
+
+
+def cpu_reference(A, B, threads: int, budget_s: float = 12.0):
+    """Time the fp32 CPU CSR loop; whole-matrix passes until budget_s, else a row sample."""
+    import oracle
+
+    vals = A.values()
+    t0 = time.perf_counter()
+    oracle.spmm_f32(A.row_ptr, A.col, vals, B, threads)
+    one = time.perf_counter() - t0
+    flops_one = 2.0 * A.nnz * B.shape[1]
+    if one > budget_s / 2:
+        return flops_one / one / 1e9, f"one full pass over all {A.nrow} rows ({one:.1f} s)"
+    reps = max(1, int(budget_s / max(one, 1e-4)))
+    reps = min(reps, 200)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        oracle.spmm_f32(A.row_ptr, A.col, vals, B, threads)
+    dt = time.perf_counter() - t0
+    return flops_one * reps / dt / 1e9, f"{reps} full passes over all {A.nrow} rows ({dt:.1f} s)"
+
+
+def run_reference(args, wl):
+    """Reference arm: rank 0 times the fp32 CPU CSR loop on all host threads.
+
+    Each step is a bounded, strided row sample of the same workload, sized so
+    the whole --warmup + --steps run stays within about two minutes."""
+    import oracle
+    import spmm_b200 as T
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    desc, build, N, dt = wl
+    A = build(T)
+    B = T.gen_dense(A.ncol, N, 1, "f32")
+    if dt != "f32":
+        B = B.astype(np.float16).astype(np.float32)
+    threads = oracle.max_threads()
+    vals = A.values()
+    t0 = time.perf_counter()
+    oracle.spmm_f32(A.row_ptr, A.col, vals, B, threads)  # one full pass: sizes the sample
+    t_full = time.perf_counter() - t0
+    per_step = min(t_full, 120.0 / (args.steps + args.warmup))
+    stride = max(1, int(round(t_full / max(per_step, 1e-6))))
+    rows = np.arange(0, A.nrow, stride, dtype=np.int64)
+    sample_nnz = int(np.diff(A.row_ptr)[rows].sum())
+    for _ in range(args.warmup):
+        oracle.spmm_f32_rows(rows, A.row_ptr, A.col, vals, B, threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.spmm_f32_rows(rows, A.row_ptr, A.col, vals, B, threads)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    value = 2.0 * sample_nnz * N / t / 1e9
+    sample = (f"every {stride}th row ({rows.shape[0]} rows, {sample_nnz} nnz) per step; "
+              f"full pass {t_full:.2f} s")
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "ms_per_step": round(2.0 * A.nnz * N / (value * 1e9) * 1e3, 4),
+            "config": {"workload": desc, "nnz": A.nnz, "M": A.nrow, "K": A.ncol, "N": N,
+                       "parallelism": "host cores (OpenMP)"},
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--workload", default="gcn", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        return run_reference(args, wl)
+
+    import torch
+    import torch.distributed as dist
+
+    import spmm_b200 as T
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"bench: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+
+    desc, build, N, dt = wl
+    tdt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[dt]
+    elem = 4 if dt == "f32" else 2
+    A = build(T)
+    M, K, nnz = A.nrow, A.ncol, A.nnz
+    Bfull = T.gen_dense(K, N, 1, dt)  # host, dt (bf16 as uint16 bits)
+    col0, ncols = T.partition_columns(N, dt, world, rank)
+    plan = T.Plan(A, N, dt, rank=rank, world=world, device=local)
+    pst = plan.stats
+    Bblk = np.ascontiguousarray(Bfull[:, col0:col0 + ncols])
+    Bh = torch.from_numpy(Bblk.view(np.int16) if dt == "bf16" else Bblk)
+    if dt == "bf16":
+        Bh = Bh.view(torch.bfloat16)
+    Bd = Bh.to(dev)
+    Cd = torch.empty((M, max(ncols, 1)), dtype=torch.float32, device=dev)[:, :ncols]
+    stream = torch.cuda.current_stream(dev)
+    in_l2 = algorithmic_bytes(M, K, nnz, ncols, elem) <= L2_BYTES
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev) if in_l2 else None
+
+    def step():
+        plan.execute1(Bd, Cd, stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- kernel-resident timing (inputs already in HBM) ----
+    for _ in range(args.warmup):
+        step()
+    plan.sync_check()
+    barrier()
+    sampler = ClockSampler(local)
+    with sampler:
+        if flush is None:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                step()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            ms_total = e0.elapsed_time(e1)
+        else:
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(args.steps)]
+            for a, b in evs:
+                flush.zero_()
+                a.record(stream)
+                step()
+                b.record(stream)
+            torch.cuda.synchronize(dev)
+            ms_total = sum(a.elapsed_time(b) for a, b in evs)
+    barrier()
+    plan.sync_check()
+    ms_step = max_over_ranks(ms_total / args.steps)
+    flops = 2.0 * nnz * N
+    value = flops / (ms_step * 1e-3) / 1e9
+
+    # ---- end to end through the public API: pinned host B -> device, execute, C -> pinned host ----
+    Bpin = Bh.pin_memory()
+    Cpin = torch.empty((M, ncols), dtype=torch.float32).pin_memory()
+    e2e_steps = max(3, min(args.steps, 50))
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        Bd.copy_(Bpin, non_blocking=True)
+        step()
+        Cpin.copy_(Cd, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    h2d = K * N * elem
+    d2h = M * N * 4
+
+    # ---- cuSPARSE baseline on this rank's block (reported, not a target) ----
+    Cs = torch.empty_like(Cd)
+    try:
+        ms_cusparse = max_over_ranks(T.cusparse_spmm(plan, Bd, Cs, warmup=3, iters=max(5, min(args.steps, 50)),
+                                                     stream=stream))
+        cs_err = float((Cs - Cd).norm() / max(Cd.norm(), 1e-30))
+    except Exception as e:  # reported
+        ms_cusparse, cs_err = None, str(e)
+    gemm = None
+    if M * K * elem <= 2**31:
+        Ad = torch.zeros((M, K), dtype=tdt, device=dev)
+        rows = torch.from_numpy(np.repeat(np.arange(M), np.diff(A.row_ptr))).to(dev)
+        Ad[rows, torch.from_numpy(A.col.astype(np.int64)).to(dev)] = torch.from_numpy(A.values()).to(dev).to(tdt)
+        Cg = torch.empty_like(Cd)
+        gemm = max_over_ranks(T.cublas_gemm(Ad, Bd, Cg, dt, warmup=3, iters=20, stream=stream))
+
+    # ---- CPU baseline (rank 0, N=1 only) ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle
+
+        Bf = Bfull.astype(np.float32) if dt != "bf16" else torch.from_numpy(Bfull.view(np.int16)).view(
+            torch.bfloat16).float().numpy()
+        threads = oracle.max_threads()
+        v, sample = cpu_reference(A, Bf, threads)
+        cpu = {"value": round(v, 3), "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+
+    peak, peak_kind = load_peaks()
+    alg = algorithmic_bytes(M, K, nnz, N, elem)
+    achieved = alg / (ms_step * 1e-3) / 1e9
+    kernels_per_step = (1 if pst["residue_row_warps"] + pst["residue_segments"] > 0 else 0) + (
+        1 if pst["tc_windows"] > 0 else 0)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": dt, "data": "synthetic",
+            "config": {"workload": desc, "M": M, "K": K, "N": N, "nnz": nnz,
+                       "parallelism": f"column shards x{world} (A replicated, no data-path collective)",
+                       "l2": "flushed between steps (2x L2 buffer)" if flush is not None
+                       else "inputs larger than L2 (126 MB)",
+                       "preprocess_ms": round(pst["preprocess_ms"], 3), "upload_ms": round(pst["upload_ms"], 3),
+                       "tc_windows": pst["tc_windows"], "residue_segments": pst["residue_segments"]},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": load_traffic(args.workload),
+                         "peak_kind": peak_kind, "algorithmic_bytes": alg,
+                         "kernel": "residue_kernel" if pst["tc_windows"] == 0 else "tc + residue"},
+            "e2e": {"value": round(flops / (ms_e2e * 1e-3) / 1e9, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 4)},
+            "baselines": {"spmm_cusparse_ms": ms_cusparse, "spmm_cusparse_rel_diff": cs_err,
+                          "gemm_cublas_ms": gemm,
+                          "spmm_cusparse_gflops": round(flops / (ms_cusparse * 1e-3) / 1e9, 3)
+                          if isinstance(ms_cusparse, float) else None},
+            "cpu_baseline": cpu,
+            "clocks": sampler.summary(),
+            "gpu_launches": kernels_per_step * args.steps * world,
+        }
+        print(json.dumps(line), flush=True)
+    plan.close()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,214 @@
+/*
+ * tcaspmm — B200-native SpMM, C = A * B, CSR A (M x K), dense row-major B (K x N),
+ * fp32 C (M x N, row-major, overwritten).  C-ABI boundary of libtcaspmm.so.
+ *
+ * Every entry point returns a tcaspmm_status (never exits), except
+ * our_spmm_balanced, which keeps the reference's void signature and its
+ * exit-on-CUDA-error behaviour.  Reference citations are paths inside the
+ * YaoLingF/SPMM tree.
+ *
+ * Threading: a plan may be executed from one host thread on one stream at a
+ * time (its scratch buffers are shared by all launches of that plan).
+ * Different plans may run concurrently.
+ */
+#ifndef TCASPMM_H
+#define TCASPMM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum tcaspmm_status {
+    TCASPMM_OK = 0,
+    TCASPMM_ERR_INVALID_ARG = 1, /* bad pointer, shape, stride or dtype */
+    TCASPMM_ERR_IO = 2,          /* file cannot be opened / written */
+    TCASPMM_ERR_FORMAT = 3,      /* malformed .smtx contents */
+    TCASPMM_ERR_ALLOC = 4,       /* host or device allocation failed */
+    TCASPMM_ERR_CUDA = 5,        /* a CUDA runtime call failed */
+    TCASPMM_ERR_UNSUPPORTED = 6, /* valid input outside the supported range */
+    TCASPMM_ERR_TIMEOUT = 7,     /* a bounded device-side wait ran out */
+    TCASPMM_ERR_NO_DEVICE = 8    /* no CUDA device (or fewer than requested) */
+} tcaspmm_status;
+
+/* Element type of B (and of the device copy of A's values). C is always fp32.
+ * fp32 runs the CUDA-core path in fp32; f16/bf16 use the tensor-core tiles for
+ * dense windows with fp32 accumulation. */
+typedef enum tcaspmm_dtype {
+    TCASPMM_F32 = 0,
+    TCASPMM_F16 = 1,
+    TCASPMM_BF16 = 2
+} tcaspmm_dtype;
+
+/* Replaces mat_format {dense, csr, coo} (src/mat_format.cuh:10-15). */
+typedef enum tcaspmm_mat_format {
+    TCASPMM_FORMAT_DENSE = 0,
+    TCASPMM_FORMAT_CSR = 1,
+    TCASPMM_FORMAT_COO = 2
+} tcaspmm_mat_format;
+
+/* Host CSR matrix.  0-based, rows in order, columns strictly ascending within a
+ * row (the convention of convert_dense_to_csr, src/miscalleneous.cu:29-65).
+ * val == NULL means a pattern matrix: every stored value is 1.0, as the .smtx
+ * loader writes them (src/file_input.cu:189).  Replaces struct CSR
+ * (src/general.cuh:125-134) with 64-bit row offsets and fp32 host values. */
+typedef struct tcaspmm_csr {
+    int64_t nrow;
+    int64_t ncol;
+    int64_t nnz;
+    int64_t *row_ptr; /* nrow + 1 */
+    int32_t *col_idx; /* nnz */
+    float *val;       /* nnz, or NULL (pattern) */
+} tcaspmm_csr;
+
+/* Layout twin of the reference's struct CSR (src/general.cuh:125-134):
+ * {int nRow, nCol, nnz; int *row_offset; int *col_idx; half *value}.
+ * `value` points at IEEE binary16 bit patterns. */
+typedef struct tcaspmm_ref_csr {
+    int nRow;
+    int nCol;
+    int nnz;
+    int *row_offset;
+    int *col_idx;
+    uint16_t *value;
+} tcaspmm_ref_csr;
+
+typedef struct tcaspmm_plan tcaspmm_plan;
+
+/* Summary of a plan (host side), for reports and tests. */
+typedef struct tcaspmm_plan_stats {
+    int64_t nrow, ncol, nnz, ncols_total;
+    int32_t num_shards;
+    int32_t window_rows;      /* rows per tensor-core window */
+    int64_t tc_windows;       /* windows run on the tensor-core tiles */
+    int64_t tc_tiles;         /* condensed column tiles over all tc windows */
+    int64_t tc_nnz;           /* nonzeros covered by tiles */
+    int64_t residue_nnz;      /* nonzeros covered by the CUDA-core kernel */
+    int64_t residue_row_warps;/* warps that each own a contiguous row range */
+    int64_t residue_segments; /* long-row segments (partial sums + fix-up) */
+    int64_t long_rows;        /* rows split into segments */
+    double preprocess_ms;     /* host preprocessing (schedule) time */
+    double upload_ms;         /* plan upload (alloc + H2D) time */
+    int64_t device_bytes;     /* device memory held by shard 0 */
+    int64_t algorithmic_bytes;/* A + B + C bytes (A: (M+1)*4 + nnz*(4+sizeof(val))) */
+} tcaspmm_plan_stats;
+
+/* ---------------------------------------------------------------- errors */
+const char *tcaspmm_status_string(tcaspmm_status s);
+/* Message describing the last failure on the calling thread ("" if none). */
+const char *tcaspmm_last_error(void);
+
+/* --------------------------------------------------------------- host CSR */
+/* Allocate a host CSR (row_ptr zeroed; val allocated when with_values != 0). */
+tcaspmm_status tcaspmm_csr_alloc(int64_t nrow, int64_t ncol, int64_t nnz, int with_values,
+                                 tcaspmm_csr *out);
+/* Free the arrays of a CSR made by this library and zero the struct. */
+tcaspmm_status tcaspmm_csr_free(tcaspmm_csr *A);
+/* Check the CSR invariants (monotone row_ptr, in-range ascending columns). */
+tcaspmm_status tcaspmm_csr_validate(const tcaspmm_csr *A);
+
+/* Read a .smtx file straight into CSR.  Format of smtx_input_to_Dense
+ * (src/file_input.cu:135-193): line 1 "M, K, nnz", line 2 the M+1 row offsets,
+ * later lines the column indices.  Values: if "<path>.val" exists (nnz
+ * little-endian float32) it is read, else A is a pattern matrix (val = NULL).
+ * Replaces smtx_input_to_Dense (src/file_input.cu:135) and the empty stub
+ * smtx_input_to_CSR (src/file_input.cu:194-196). */
+tcaspmm_status tcaspmm_smtx_read(const char *path, tcaspmm_csr *out);
+/* Write A as .smtx (and "<path>.val" when A->val != NULL). */
+tcaspmm_status tcaspmm_smtx_write(const char *path, const tcaspmm_csr *A);
+
+/* Dense row-major M x K binary16 matrix -> CSR, dropping zeros.
+ * Replaces convert_dense_to_csr (src/miscalleneous.cu:29-65). */
+tcaspmm_status tcaspmm_dense_to_csr(const uint16_t *dense, int64_t M, int64_t K, tcaspmm_csr *out);
+
+/* ----------------------------------------------------- seeded generators
+ * Counter-based SplitMix64 streams: every value depends only on (seed, index),
+ * so results are identical for any thread count.  Replaces the unseeded
+ * prepare_cpu_matrix (src/general.cuh:140-174). */
+/* rows x cols N(0,1) values rounded to dt, written to out (row-major, ld = cols). */
+tcaspmm_status tcaspmm_gen_dense(int64_t rows, int64_t cols, uint64_t seed, tcaspmm_dtype dt,
+                                 void *out);
+/* Each entry kept with probability density, values N(0,1). */
+tcaspmm_status tcaspmm_gen_uniform(int64_t M, int64_t K, double density, uint64_t seed,
+                                   tcaspmm_csr *out);
+/* Magnitude pruning: W = s_i * Z_ij, s_i ~ LogNormal(0, 0.5), Z ~ N(0,1); keep
+ * the globally largest (1 - sparsity) fraction of |W|; values are W. */
+tcaspmm_status tcaspmm_gen_magnitude(int64_t M, int64_t K, double sparsity, uint64_t seed,
+                                     tcaspmm_csr *out);
+/* R-MAT(a, b, c) graph on 2^scale nodes with `edges` directed draws.
+ * kind 0 (GCN): symmetrise, add self-loops, dedupe, values 1/sqrt(d_i d_j).
+ * kind 1 (SAGE mean): dedupe directed edges, values 1/deg(i). */
+tcaspmm_status tcaspmm_gen_rmat(int scale, int64_t edges, double a, double b, double c, int kind,
+                                uint64_t seed, tcaspmm_csr *out);
+/* Extreme skew: n x n, `hubs` rows (evenly spaced) with hub_nnz distinct uniform
+ * columns, every other row Poisson(lambda) uniform columns; values U(-1, 1). */
+tcaspmm_status tcaspmm_gen_skew(int64_t n, int64_t hubs, int64_t hub_nnz, double lambda,
+                                uint64_t seed, tcaspmm_csr *out);
+
+/* --------------------------------------------------------- multi-GPU split
+ * Column partition of B and C over `world` GPUs: contiguous blocks of
+ * ceil(N / world) columns rounded up to a 16-byte multiple of dt. */
+tcaspmm_status tcaspmm_partition_columns(int64_t N, tcaspmm_dtype dt, int world, int rank,
+                                         int64_t *col_begin, int64_t *col_count);
+
+/* ------------------------------------------------------------------ plans
+ * A plan holds the preprocessed schedule of A and every device buffer the
+ * kernels read (A's CSR arrays, the schedule, tensor-core tiles, scratch).
+ * Replaces workload_manager (src/our_spmm.cu:353-477) and the per-call device
+ * setup of our_spmm_balanced (src/our_spmm.cu:486-550). */
+
+/* One plan over num_gpus devices (devices[i], or 0..num_gpus-1 when NULL); the
+ * N columns are split by tcaspmm_partition_columns. */
+tcaspmm_status tcaspmm_plan_create(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt, int num_gpus,
+                                   const int *devices, tcaspmm_plan **out);
+/* One process per GPU: a plan for rank's column block only, on `device`. */
+tcaspmm_status tcaspmm_plan_create_shard(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt, int rank,
+                                         int world, int device, tcaspmm_plan **out);
+tcaspmm_status tcaspmm_plan_destroy(tcaspmm_plan *plan);
+tcaspmm_status tcaspmm_plan_get_stats(const tcaspmm_plan *plan, tcaspmm_plan_stats *out);
+/* Shard s of the plan: its device and its column block [col_begin, col_begin + col_count). */
+tcaspmm_status tcaspmm_plan_shard(const tcaspmm_plan *plan, int shard, int *device,
+                                  int64_t *col_begin, int64_t *col_count);
+
+/* Run C = A * B on every shard.  Per shard s: dB[s] is the device K x col_count
+ * block of B with leading dimension ldb[s] (elements), dC[s] the device M x
+ * col_count block of C with leading dimension ldc[s], streams[s] a cudaStream_t
+ * (NULL = legacy default stream).  Asynchronous: returns after the launches. */
+tcaspmm_status tcaspmm_execute(tcaspmm_plan *plan, const void *const *dB, const int64_t *ldb,
+                               float *const *dC, const int64_t *ldc, void *const *streams);
+/* Single-shard convenience form of tcaspmm_execute. */
+tcaspmm_status tcaspmm_execute1(tcaspmm_plan *plan, const void *dB, int64_t ldb, float *dC,
+                                int64_t ldc, void *stream);
+/* Wait for the plan's shards and report a device-side error (a bounded wait
+ * that ran out in a tensor-core kernel) as TCASPMM_ERR_TIMEOUT. */
+tcaspmm_status tcaspmm_plan_sync_check(tcaspmm_plan *plan);
+
+/* ------------------------------------------------- schedule inspection
+ * Build the host schedule without touching a GPU and report, for every
+ * nonzero j of A, how many work units cover it (cover[j], must be 1) and which
+ * kind covers it (kind[j]: 1 residue row, 2 residue segment, 3 tensor-core tile
+ * cell).  Tile cells are also checked against A's column and value. */
+tcaspmm_status tcaspmm_schedule_coverage(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt,
+                                         int32_t *cover, int8_t *kind, tcaspmm_plan_stats *stats);
+
+/* ------------------------------------------------- reference entry point
+ * Same signature, argument meaning and behaviour as our_spmm_balanced
+ * (src/our_spmm.cuh:4, src/our_spmm.cu:478-594): host CSR with binary16 values,
+ * host binary16 B (K x N), host fp32 C (M x N) overwritten; allocates device
+ * memory, copies in, preprocesses, runs 5 warm-up and n_iter timed launches,
+ * copies C back, frees, and stores the average kernel milliseconds in
+ * *elapsed (if not NULL).  On a CUDA error it prints the error and exits, as
+ * CHECK_CUDA does (src/general.cuh:8-16). */
+void our_spmm_balanced(tcaspmm_ref_csr *A_csr, uint16_t *B, float *C, int M, int N, int K,
+                       int n_iter, double *elapsed);
+/* Status-returning form of our_spmm_balanced (no exit). */
+tcaspmm_status tcaspmm_our_spmm_balanced(const tcaspmm_ref_csr *A_csr, const uint16_t *B, float *C,
+                                         int M, int N, int K, int n_iter, double *elapsed);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TCASPMM_H */

@@ -1,0 +1,39 @@
+/*
+ * Library baselines reported beside tcaspmm (never on its hot path), in
+ * libtcaspmm_baselines.so.  Both time `iters` launches with CUDA events on
+ * `stream` after `warmup` untimed launches and return the average ms.
+ */
+#ifndef TCASPMM_BASELINES_H
+#define TCASPMM_BASELINES_H
+
+#include "tcaspmm.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cusparseSpMM on a device CSR (int32 offsets/indices, values in dt), row-major
+ * B (K x N, ld ldb) in dt, fp32 C (M x N, ld ldc), fp32 compute,
+ * CUSPARSE_SPMM_ALG_DEFAULT.  Replaces perform_cuSPARSE_SpMM
+ * (src/spmm_cusparse.cu:446-580) minus its host conversion and copies. */
+tcaspmm_status tcaspmm_cusparse_spmm(const int32_t *d_row_ptr, const int32_t *d_col, const void *d_val, int64_t M,
+                                     int64_t K, int64_t nnz, const void *dB, int64_t ldb, float *dC, int64_t ldc,
+                                     int64_t N, tcaspmm_dtype dt, int warmup, int iters, void *stream,
+                                     double *ms_per_iter);
+
+/* Dense cublasGemmEx: C (M x N, fp32) = A (M x K, row-major, dt) * B (K x N,
+ * row-major, dt), computed as C^T = B^T A^T in column-major with
+ * CUBLAS_COMPUTE_32F, as perform_GemmEx does (src/gemm_cublas.cu:60-67). */
+tcaspmm_status tcaspmm_cublas_gemm(const void *dA, const void *dB, float *dC, int64_t M, int64_t N, int64_t K,
+                                   tcaspmm_dtype dt, int warmup, int iters, void *stream, double *ms_per_iter);
+
+/* Device CSR arrays that a plan uploaded for `shard` (int32 offsets, int32
+ * columns, values in the plan's dtype); lets a baseline run on the same bytes. */
+tcaspmm_status tcaspmm_plan_device_csr(const tcaspmm_plan *plan, int shard, const int32_t **row_ptr,
+                                       const int32_t **col, const void **val);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TCASPMM_BASELINES_H */

@@ -1,0 +1,418 @@
+// Plans: host schedule -> device buffers per shard, and kernel launches.
+//
+// Replaces the device half of our_spmm_balanced (src/our_spmm.cu:486-565):
+// the reference allocates and uploads A, B, C and three schedule arrays per
+// call and launches kernel_our_spmm_balanced<64> on the default stream.  A plan
+// uploads A and its schedule once; execute only launches (on caller streams).
+#include <algorithm>
+#include <chrono>
+#include <cstring>
+#include <memory>
+#include <vector>
+
+#include <cuda_runtime.h>
+#include <omp.h>
+
+#include "internal.h"
+#include "plan.h"
+#include "residue.cuh"
+
+using namespace tca;
+
+namespace tca {
+
+tcaspmm_status cuda_fail(cudaError_t e, const char *what)
+{
+    return fail(TCASPMM_ERR_CUDA, "%s: %s (%d)", what, cudaGetErrorString(e), (int)e);
+}
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev)
+    {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard()
+    {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+template <typename X>
+tcaspmm_status upload(Shard &sh, X **dst, const X *src, size_t n, const char *what)
+{
+    *dst = nullptr;
+    if (n == 0) return TCASPMM_OK;
+    cudaError_t e = cudaMalloc((void **)dst, sizeof(X) * n);
+    if (e != cudaSuccess) {
+        *dst = nullptr;
+        return fail(TCASPMM_ERR_ALLOC, "cudaMalloc of %zu bytes for %s failed: %s", sizeof(X) * n, what,
+                    cudaGetErrorString(e));
+    }
+    sh.allocs.push_back(*dst);
+    sh.bytes += (int64_t)(sizeof(X) * n);
+    if (src) {
+        e = cudaMemcpy(*dst, src, sizeof(X) * n, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return cuda_fail(e, what);
+    }
+    return TCASPMM_OK;
+}
+
+// Round fp32 host values to the device dtype.
+std::vector<uint16_t> to_16bit(const float *v, int64_t n, tcaspmm_dtype dt)
+{
+    std::vector<uint16_t> out((size_t)n);
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; i++)
+        out[i] = dt == TCASPMM_F16 ? float_to_half_bits(v[i]) : float_to_bf16_bits(v[i]);
+    return out;
+}
+
+tcaspmm_status build_shard(const tcaspmm_csr &A, tcaspmm_dtype dt, int device, int64_t col_begin,
+                           int64_t ncols, Shard *sh, double *prep_ms)
+{
+    sh->device = device;
+    sh->col_begin = col_begin;
+    sh->ncols = ncols;
+    DeviceGuard g(device);
+    int nsm = 148;
+    cudaError_t e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess) return cuda_fail(e, "query SM count");
+
+    ScheduleOptions opt;
+    opt.num_sms = nsm;
+    opt.allow_tc = tc_supported();
+    tcaspmm_status s = build_schedule(A, ncols, dt, opt, &sh->sched);
+    if (s != TCASPMM_OK) return s;
+    *prep_ms += sh->sched.build_ms;
+    const Schedule &S = sh->sched;
+
+    // A in CSR: int32 row offsets, int32 columns, values in dt.
+    std::vector<int32_t> rp32((size_t)A.nrow + 1);
+    for (int64_t i = 0; i <= A.nrow; i++) rp32[i] = (int32_t)A.row_ptr[i];
+    if ((s = upload(*sh, &sh->row_ptr, rp32.data(), rp32.size(), "row offsets")) != TCASPMM_OK) return s;
+    if ((s = upload(*sh, &sh->col, A.col_idx, (size_t)A.nnz, "column indices")) != TCASPMM_OK) return s;
+    {
+        std::vector<float> ones;
+        const float *v = A.val;
+        if (!v) {
+            ones.assign((size_t)A.nnz, 1.0f);
+            v = ones.data();
+        }
+        if (dt == TCASPMM_F32) {
+            float *d = nullptr;
+            if ((s = upload(*sh, &d, v, (size_t)A.nnz, "values")) != TCASPMM_OK) return s;
+            sh->val = d;
+        } else {
+            std::vector<uint16_t> h = to_16bit(v, A.nnz, dt);
+            uint16_t *d = nullptr;
+            if ((s = upload(*sh, &d, h.data(), h.size(), "values")) != TCASPMM_OK) return s;
+            sh->val = d;
+        }
+    }
+    // Residue schedule and its scratch (partials + counters).
+    const ResidueSchedule &RS = S.res;
+    static_assert(sizeof(Int2) == sizeof(int2) && sizeof(Int4) == sizeof(int4), "layout");
+    if ((s = upload(*sh, (Int2 **)&sh->ranges, RS.ranges.data(), RS.ranges.size(), "row ranges")) != TCASPMM_OK) return s;
+    if ((s = upload(*sh, (Int4 **)&sh->segs, RS.segs.data(), RS.segs.size(), "segments")) != TCASPMM_OK) return s;
+    if ((s = upload(*sh, (Int4 **)&sh->longs, RS.longs.data(), RS.longs.size(), "long rows")) != TCASPMM_OK) return s;
+    sh->n_ranges = (int)RS.ranges.size();
+    sh->n_segs = (int)RS.segs.size();
+    sh->n_longs = (int)RS.longs.size();
+    sh->long_thr = RS.long_thr;
+    sh->pstride = (int)((ncols + 3) / 4 * 4);
+    if ((s = upload<float>(*sh, &sh->partials, nullptr, (size_t)sh->n_segs * sh->pstride, "partials")) != TCASPMM_OK) return s;
+    if ((s = upload<unsigned int>(*sh, &sh->counters, nullptr, (size_t)sh->n_longs, "counters")) != TCASPMM_OK) return s;
+    if (sh->n_longs) {
+        e = cudaMemset(sh->counters, 0, sizeof(unsigned int) * sh->n_longs);
+        if (e != cudaSuccess) return cuda_fail(e, "zero counters");
+    }
+    if ((s = upload<int>(*sh, &sh->err, nullptr, 1, "error word")) != TCASPMM_OK) return s;
+    e = cudaMemset(sh->err, 0, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "zero error word");
+    if ((s = tc_upload(A, dt, sh)) != TCASPMM_OK) return s;
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "plan upload");
+    return TCASPMM_OK;
+}
+
+template <typename T, int VEC, int G>
+void launch_res(const ResidueParams &p, int total_warps, cudaStream_t st)
+{
+    const int blocks = (total_warps + 7) / 8;
+    residue_kernel<T, VEC, G, 8><<<blocks, 256, 0, st>>>(p);
+}
+
+template <typename T, int VEC>
+void launch_res_g(int G, const ResidueParams &p, int total_warps, cudaStream_t st)
+{
+    switch (G) {
+    case 1: launch_res<T, VEC, 1>(p, total_warps, st); break;
+    case 2: launch_res<T, VEC, 2>(p, total_warps, st); break;
+    case 4: launch_res<T, VEC, 4>(p, total_warps, st); break;
+    case 8: launch_res<T, VEC, 8>(p, total_warps, st); break;
+    case 16: launch_res<T, VEC, 16>(p, total_warps, st); break;
+    default: launch_res<T, VEC, 32>(p, total_warps, st); break;
+    }
+}
+
+template <typename T>
+void launch_res_t(bool vec, int G, const ResidueParams &p, int total_warps, cudaStream_t st)
+{
+    if (vec)
+        launch_res_g<T, 16 / sizeof(T)>(G, p, total_warps, st);
+    else
+        launch_res_g<T, 1>(G, p, total_warps, st);
+}
+
+}  // namespace
+
+tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB, int64_t ldb, float *dC,
+                              int64_t ldc, cudaStream_t st)
+{
+    const int total = sh.n_segs + sh.n_ranges;
+    if (total == 0 || sh.ncols == 0) return TCASPMM_OK;
+    const int elem = dtype_size(dt);
+    // 16-byte vector path needs 16-byte aligned B and C rows.
+    const bool vec = ((uintptr_t)dB % 16 == 0) && ((ldb * elem) % 16 == 0) && ((uintptr_t)dC % 16 == 0) &&
+                     (ldc % 4 == 0) && (sh.ncols % (16 / elem) == 0);
+    int G, VEC;
+    residue_shape(sh.ncols, dt, vec, &G, &VEC);
+    // The row ranges were cut for the vector shape; the scalar path uses the
+    // same ranges with its own G (more passes), which stays correct.
+    ResidueParams p;
+    p.row_ptr = sh.row_ptr;
+    p.col = sh.col;
+    p.val = sh.val;
+    p.B = dB;
+    p.ldb = ldb;
+    p.C = dC;
+    p.ldc = ldc;
+    p.ncols = (int)sh.ncols;
+    p.ranges = (const int2 *)sh.ranges;
+    p.n_ranges = sh.n_ranges;
+    p.segs = (const int4 *)sh.segs;
+    p.n_segs = sh.n_segs;
+    p.longs = (const int4 *)sh.longs;
+    p.partials = sh.partials;
+    p.pstride = sh.pstride;
+    p.counters = sh.counters;
+    p.long_thr = sh.long_thr;
+    if (dt == TCASPMM_F32)
+        launch_res_t<float>(vec, G, p, total, st);
+    else if (dt == TCASPMM_F16)
+        launch_res_t<__half>(vec, G, p, total, st);
+    else
+        launch_res_t<__nv_bfloat16>(vec, G, p, total, st);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "residue kernel launch");
+    return TCASPMM_OK;
+}
+
+void free_shard(Shard &sh)
+{
+    if (sh.allocs.empty()) return;
+    DeviceGuard g(sh.device);
+    for (void *p : sh.allocs) cudaFree(p);
+    sh.allocs.clear();
+}
+
+}  // namespace tca
+
+struct tcaspmm_plan {
+    int64_t M = 0, K = 0, nnz = 0, N = 0;
+    tcaspmm_dtype dt = TCASPMM_F32;
+    std::vector<std::unique_ptr<Shard>> shards;
+    tcaspmm_plan_stats stats{};
+    ~tcaspmm_plan()
+    {
+        for (auto &s : shards) free_shard(*s);
+    }
+};
+
+static tcaspmm_status create_common(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt,
+                                    const std::vector<int> &devices, const std::vector<int64_t> &begins,
+                                    const std::vector<int64_t> &counts, tcaspmm_plan **out)
+{
+    auto t0 = std::chrono::steady_clock::now();
+    std::unique_ptr<tcaspmm_plan> P(new tcaspmm_plan());
+    P->M = A->nrow;
+    P->K = A->ncol;
+    P->nnz = A->nnz;
+    P->N = N;
+    P->dt = dt;
+    double prep = 0.0;
+    for (size_t i = 0; i < devices.size(); i++) {
+        P->shards.emplace_back(new Shard());
+        tcaspmm_status s = build_shard(*A, dt, devices[i], begins[i], counts[i], P->shards.back().get(), &prep);
+        if (s != TCASPMM_OK) return s;
+    }
+    const double total = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    tcaspmm_plan_stats &st = P->stats;
+    const Schedule &S = P->shards[0]->sched;
+    st.nrow = A->nrow;
+    st.ncol = A->ncol;
+    st.nnz = A->nnz;
+    st.ncols_total = N;
+    st.num_shards = (int32_t)P->shards.size();
+    st.window_rows = S.tc.R;
+    st.tc_windows = (int64_t)S.tc.windows.size();
+    st.tc_tiles = S.tc.KT ? (int64_t)S.tc.tile_cols.size() / S.tc.KT : 0;
+    st.tc_nnz = S.tc.nnz;
+    st.residue_nnz = S.res.nnz;
+    st.residue_row_warps = (int64_t)S.res.ranges.size();
+    st.residue_segments = (int64_t)S.res.segs.size();
+    st.long_rows = (int64_t)S.res.longs.size();
+    st.preprocess_ms = prep;
+    st.upload_ms = total - prep;
+    st.device_bytes = P->shards[0]->bytes;
+    st.algorithmic_bytes = algorithmic_bytes(A->nrow, A->ncol, A->nnz, N, dt);
+    *out = P.release();
+    return TCASPMM_OK;
+}
+
+static tcaspmm_status check_inputs(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt, tcaspmm_plan **out)
+{
+    if (!out) return fail(TCASPMM_ERR_INVALID_ARG, "plan_create: out is NULL");
+    *out = nullptr;
+    if (!A) return fail(TCASPMM_ERR_INVALID_ARG, "plan_create: A is NULL");
+    if (!dtype_valid(dt)) return fail(TCASPMM_ERR_INVALID_ARG, "plan_create: unknown dtype %d", (int)dt);
+    if (N < 0 || N > INT32_MAX) return fail(TCASPMM_ERR_INVALID_ARG, "plan_create: N=%lld out of range", (long long)N);
+    return tcaspmm_csr_validate(A);
+}
+
+extern "C" {
+
+tcaspmm_status tcaspmm_plan_create(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt, int num_gpus,
+                                   const int *devices, tcaspmm_plan **out)
+{
+    clear_error();
+    tcaspmm_status s = check_inputs(A, N, dt, out);
+    if (s != TCASPMM_OK) return s;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return fail(TCASPMM_ERR_NO_DEVICE, "no CUDA device");
+    }
+    if (num_gpus < 1) return fail(TCASPMM_ERR_INVALID_ARG, "num_gpus=%d", num_gpus);
+    std::vector<int> devs(num_gpus);
+    std::vector<int64_t> b(num_gpus), c(num_gpus);
+    for (int i = 0; i < num_gpus; i++) {
+        devs[i] = devices ? devices[i] : i;
+        if (devs[i] < 0 || devs[i] >= ndev)
+            return fail(TCASPMM_ERR_NO_DEVICE, "device %d requested, %d present", devs[i], ndev);
+        tcaspmm_partition_columns(N, dt, num_gpus, i, &b[i], &c[i]);
+    }
+    return create_common(A, N, dt, devs, b, c, out);
+}
+
+tcaspmm_status tcaspmm_plan_create_shard(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt, int rank, int world,
+                                         int device, tcaspmm_plan **out)
+{
+    clear_error();
+    tcaspmm_status s = check_inputs(A, N, dt, out);
+    if (s != TCASPMM_OK) return s;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return fail(TCASPMM_ERR_NO_DEVICE, "no CUDA device");
+    }
+    if (device < 0 || device >= ndev) return fail(TCASPMM_ERR_NO_DEVICE, "device %d requested, %d present", device, ndev);
+    int64_t b, c;
+    s = tcaspmm_partition_columns(N, dt, world, rank, &b, &c);
+    if (s != TCASPMM_OK) return s;
+    return create_common(A, N, dt, {device}, {b}, {c}, out);
+}
+
+tcaspmm_status tcaspmm_plan_destroy(tcaspmm_plan *plan)
+{
+    delete plan;
+    return TCASPMM_OK;
+}
+
+tcaspmm_status tcaspmm_plan_get_stats(const tcaspmm_plan *plan, tcaspmm_plan_stats *out)
+{
+    if (!plan || !out) return fail(TCASPMM_ERR_INVALID_ARG, "plan_get_stats: NULL argument");
+    *out = plan->stats;
+    return TCASPMM_OK;
+}
+
+tcaspmm_status tcaspmm_plan_shard(const tcaspmm_plan *plan, int shard, int *device, int64_t *col_begin,
+                                  int64_t *col_count)
+{
+    if (!plan || shard < 0 || shard >= (int)plan->shards.size())
+        return fail(TCASPMM_ERR_INVALID_ARG, "plan_shard: bad shard %d", shard);
+    const Shard &s = *plan->shards[shard];
+    if (device) *device = s.device;
+    if (col_begin) *col_begin = s.col_begin;
+    if (col_count) *col_count = s.ncols;
+    return TCASPMM_OK;
+}
+
+tcaspmm_status tcaspmm_execute(tcaspmm_plan *plan, const void *const *dB, const int64_t *ldb, float *const *dC,
+                               const int64_t *ldc, void *const *streams)
+{
+    if (!plan || !dB || !ldb || !dC || !ldc) return fail(TCASPMM_ERR_INVALID_ARG, "execute: NULL argument");
+    for (size_t i = 0; i < plan->shards.size(); i++) {
+        const Shard &sh = *plan->shards[i];
+        if (sh.ncols == 0 || plan->M == 0) continue;
+        if (ldb[i] < sh.ncols || ldc[i] < sh.ncols)
+            return fail(TCASPMM_ERR_INVALID_ARG, "execute: shard %zu ldb=%lld ldc=%lld below %lld columns", i,
+                        (long long)ldb[i], (long long)ldc[i], (long long)sh.ncols);
+        if (!dC[i] || (!dB[i] && plan->K > 0))
+            return fail(TCASPMM_ERR_INVALID_ARG, "execute: shard %zu has a NULL B or C", i);
+        cudaStream_t st = streams ? (cudaStream_t)streams[i] : (cudaStream_t)0;
+        DeviceGuard g(sh.device);
+        tcaspmm_status s = launch_tc(sh, plan->dt, dB[i], ldb[i], dC[i], ldc[i], st);
+        if (s != TCASPMM_OK) return s;
+        s = launch_residue(sh, plan->dt, dB[i], ldb[i], dC[i], ldc[i], st);
+        if (s != TCASPMM_OK) return s;
+    }
+    return TCASPMM_OK;
+}
+
+tcaspmm_status tcaspmm_execute1(tcaspmm_plan *plan, const void *dB, int64_t ldb, float *dC, int64_t ldc, void *stream)
+{
+    if (!plan) return fail(TCASPMM_ERR_INVALID_ARG, "execute1: plan is NULL");
+    if (plan->shards.size() != 1)
+        return fail(TCASPMM_ERR_INVALID_ARG, "execute1: plan has %zu shards", plan->shards.size());
+    return tcaspmm_execute(plan, &dB, &ldb, &dC, &ldc, &stream);
+}
+
+tcaspmm_status tcaspmm_plan_sync_check(tcaspmm_plan *plan)
+{
+    if (!plan) return fail(TCASPMM_ERR_INVALID_ARG, "plan_sync_check: plan is NULL");
+    for (auto &up : plan->shards) {
+        Shard &sh = *up;
+        DeviceGuard g(sh.device);
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return cuda_fail(e, "synchronize");
+        int err = 0;
+        e = cudaMemcpy(&err, sh.err, sizeof(int), cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) return cuda_fail(e, "read error word");
+        if (err != 0) {
+            cudaMemset(sh.err, 0, sizeof(int));
+            return fail(TCASPMM_ERR_TIMEOUT, "device %d: tensor-core kernel gave up waiting (code 0x%x)", sh.device, err);
+        }
+    }
+    return TCASPMM_OK;
+}
+
+}  // extern "C"
+
+// Device CSR arrays of a shard, for baselines that run on the same upload.
+extern "C" tcaspmm_status tcaspmm_plan_device_csr(const tcaspmm_plan *plan, int shard, const int32_t **row_ptr,
+                                                  const int32_t **col, const void **val)
+{
+    if (!plan || shard < 0 || shard >= (int)plan->shards.size())
+        return fail(TCASPMM_ERR_INVALID_ARG, "plan_device_csr: bad shard");
+    const Shard &s = *plan->shards[shard];
+    if (row_ptr) *row_ptr = s.row_ptr;
+    if (col) *col = s.col;
+    if (val) *val = s.val;
+    return TCASPMM_OK;
+}

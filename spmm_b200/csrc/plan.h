@@ -1,0 +1,54 @@
+// Per-device state of a plan and the launchers shared by plan.cu and tc.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <vector>
+
+#include "internal.h"
+
+namespace tca {
+
+struct Shard {
+    int device = 0;
+    int64_t col_begin = 0, ncols = 0;
+    Schedule sched;  // host schedule; large arrays are released after upload
+    std::vector<void *> allocs;
+    int64_t bytes = 0;
+
+    // A in CSR on the device.
+    int32_t *row_ptr = nullptr;
+    int32_t *col = nullptr;
+    void *val = nullptr;
+
+    // Residue schedule + scratch.
+    Int2 *ranges = nullptr;
+    Int4 *segs = nullptr;
+    Int4 *longs = nullptr;
+    int n_ranges = 0, n_segs = 0, n_longs = 0;
+    int long_thr = 0;
+    float *partials = nullptr;
+    int pstride = 0;
+    unsigned int *counters = nullptr;
+
+    // Tensor-core windows.
+    int n_windows = 0;
+    Int4 *tc_windows = nullptr;  // {first row, first tile, tiles, rows}
+    int32_t *tc_cols = nullptr;  // KT B-row indices per tile
+    void *tc_vals = nullptr;     // R x KT values per tile, shared-memory image
+
+    int *err = nullptr;  // device error word (bounded waits that ran out)
+};
+
+tcaspmm_status cuda_fail(cudaError_t e, const char *what);
+void free_shard(Shard &sh);
+
+// Tensor-core path (tc.cu).
+bool tc_supported();
+tcaspmm_status tc_upload(const tcaspmm_csr &A, tcaspmm_dtype dt, Shard *sh);
+tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int64_t ldb, float *dC, int64_t ldc,
+                         cudaStream_t st);
+tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB, int64_t ldb, float *dC,
+                              int64_t ldc, cudaStream_t st);
+
+}  // namespace tca

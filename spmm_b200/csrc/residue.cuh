@@ -1,0 +1,247 @@
+// CUDA-core residue kernel: C rows that are not covered by tensor-core windows.
+//
+// Replaces the short-row / long-row paths of kernel_our_spmm_balanced
+// (multirow_per_tb src/our_spmm.cu:24-160, multitb_per_row :161-295), which
+// push each nonzero through a 1/8-useful mma.sync.m16n8k8 after a shared-memory
+// transpose.  Here a nonzero is one 16-byte B load per lane and VEC fp32 FMAs:
+//   * a lane group of G lanes (power of two) covers G*VEC columns of one B row
+//     with 16-byte loads (VEC = 4 fp32 or 8 fp16/bf16); a warp holds P = 32/G
+//     groups, and columns beyond G*VEC are covered by extra passes;
+//   * row warps: each group walks its rows of a contiguous row range (group s
+//     takes rows s, s+P, ...) with U independent B loads in flight per lane and
+//     writes each finished C row with streaming 16-byte stores;
+//   * segment warps: the P groups split one segment of a long row, reduce with
+//     __shfl_xor_sync, and store a partial row; the warp that completes a long
+//     row's last segment (atomic counter) sums all its partials in segment
+//     order and writes C, so the result does not depend on timing.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+#include <type_traits>
+
+namespace tca {
+
+struct ResidueParams {
+    const int32_t *__restrict__ row_ptr;
+    const int32_t *__restrict__ col;
+    const void *__restrict__ val;
+    const void *__restrict__ B;
+    long long ldb;
+    float *__restrict__ C;
+    long long ldc;
+    int ncols;
+    const int2 *__restrict__ ranges;
+    int n_ranges;
+    const int4 *__restrict__ segs;   // {row, begin, end, long id}
+    int n_segs;
+    const int4 *__restrict__ longs;  // {row, first seg, number of segs, 0}
+    float *partials;                 // n_segs x pstride
+    int pstride;
+    unsigned int *counters;          // one per long row, zero between launches
+    int long_thr;
+};
+
+template <typename T> __device__ __forceinline__ float to_f(T x);
+template <> __device__ __forceinline__ float to_f<float>(float x) { return x; }
+template <> __device__ __forceinline__ float to_f<__half>(__half x) { return __half2float(x); }
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+// Raw 16-byte (or one-element) load of a B row slice, converted at FMA time.
+template <typename T, int VEC> struct Raw { uint4 u; };
+template <typename T> struct Raw<T, 1> { T s; };
+
+template <typename T, int VEC>
+__device__ __forceinline__ void load_raw(const T *p, Raw<T, VEC> &r)
+{
+    if constexpr (VEC == 1)
+        r.s = __ldg(p);
+    else
+        r.u = __ldg(reinterpret_cast<const uint4 *>(p));
+}
+
+template <typename T, int VEC>
+__device__ __forceinline__ void zero_raw(Raw<T, VEC> &r)
+{
+    if constexpr (VEC == 1)
+        r.s = T(0.0f);
+    else
+        r.u = make_uint4(0u, 0u, 0u, 0u);
+}
+
+template <typename T, int VEC>
+__device__ __forceinline__ void fma_raw(float v, const Raw<T, VEC> &r, float (&acc)[VEC])
+{
+    if constexpr (VEC == 1) {
+        acc[0] = fmaf(v, to_f<T>(r.s), acc[0]);
+    } else if constexpr (sizeof(T) == 4) {
+        const float *f = reinterpret_cast<const float *>(&r.u);
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) acc[k] = fmaf(v, f[k], acc[k]);
+    } else if constexpr (std::is_same<T, __half>::value) {
+        const __half2 *h = reinterpret_cast<const __half2 *>(&r.u);
+#pragma unroll
+        for (int k = 0; k < VEC / 2; ++k) {
+            const float2 f = __half22float2(h[k]);
+            acc[2 * k] = fmaf(v, f.x, acc[2 * k]);
+            acc[2 * k + 1] = fmaf(v, f.y, acc[2 * k + 1]);
+        }
+    } else {
+        const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&r.u);
+#pragma unroll
+        for (int k = 0; k < VEC / 2; ++k) {
+            const float2 f = __bfloat1622float2(h[k]);
+            acc[2 * k] = fmaf(v, f.x, acc[2 * k]);
+            acc[2 * k + 1] = fmaf(v, f.y, acc[2 * k + 1]);
+        }
+    }
+}
+
+// Streaming (evict-first) store of VEC fp32 results: C is written once and
+// should not push B rows out of L2.
+template <int VEC>
+__device__ __forceinline__ void store_c(float *c, const float (&a)[VEC])
+{
+    if constexpr (VEC == 1) {
+        __stcs(c, a[0]);
+    } else {
+#pragma unroll
+        for (int k = 0; k < VEC; k += 4)
+            __stcs(reinterpret_cast<float4 *>(c + k), make_float4(a[k], a[k + 1], a[k + 2], a[k + 3]));
+    }
+}
+
+template <int VEC>
+__device__ __forceinline__ void store_l2(float *c, const float (&a)[VEC])
+{
+    if constexpr (VEC == 1) {
+        __stcg(c, a[0]);
+    } else {
+#pragma unroll
+        for (int k = 0; k < VEC; k += 4)
+            __stcg(reinterpret_cast<float4 *>(c + k), make_float4(a[k], a[k + 1], a[k + 2], a[k + 3]));
+    }
+}
+
+template <int VEC>
+__device__ __forceinline__ void add_l2(const float *c, float (&a)[VEC])
+{
+    if constexpr (VEC == 1) {
+        a[0] += __ldcg(c);
+    } else {
+#pragma unroll
+        for (int k = 0; k < VEC; k += 4) {
+            const float4 x = __ldcg(reinterpret_cast<const float4 *>(c + k));
+            a[k] += x.x;
+            a[k + 1] += x.y;
+            a[k + 2] += x.z;
+            a[k + 3] += x.w;
+        }
+    }
+}
+
+// acc += sum_{j = b, b+stride, ... < e} val[j] * B[col[j]][c0 .. c0+VEC).
+// The U column indices of a step are read first, then U independent B loads
+// are issued, then the FMAs, so each lane keeps U loads in flight.
+template <typename T, int VEC, int U>
+__device__ __forceinline__ void accumulate(const ResidueParams &p, int b, int e, int stride, int c0,
+                                           float (&acc)[VEC])
+{
+    const T *__restrict__ B = static_cast<const T *>(p.B) + c0;
+    const T *__restrict__ val = static_cast<const T *>(p.val);
+    for (int j = b; j < e; j += U * stride) {
+        int cc[U];
+        float vv[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int jj = j + u * stride;
+            const bool ok = jj < e;
+            cc[u] = ok ? __ldg(p.col + jj) : -1;
+            vv[u] = ok ? to_f<T>(__ldg(val + jj)) : 0.0f;
+        }
+        Raw<T, VEC> rb[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            if (cc[u] >= 0)
+                load_raw<T, VEC>(B + (long long)cc[u] * p.ldb, rb[u]);
+            else
+                zero_raw<T, VEC>(rb[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) fma_raw<T, VEC>(vv[u], rb[u], acc);
+    }
+}
+
+template <typename T, int VEC, int G, int U>
+__global__ void __launch_bounds__(256) residue_kernel(const ResidueParams p)
+{
+    constexpr int P = 32 / G;
+    constexpr int CPP = G * VEC;  // columns per pass
+    const int lane = threadIdx.x & 31;
+    const int warp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    const int sub = lane / G, gl = lane % G;
+    const int npass = (p.ncols + CPP - 1) / CPP;
+
+    if (warp < p.n_segs) {
+        const int4 s = p.segs[warp];
+        for (int pass = 0; pass < npass; ++pass) {
+            const int c0 = pass * CPP + gl * VEC;
+            float acc[VEC];
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
+            if (c0 < p.ncols) accumulate<T, VEC, U>(p, s.y + sub, s.z, P, c0, acc);
+#pragma unroll
+            for (int off = G; off < 32; off <<= 1)
+#pragma unroll
+                for (int k = 0; k < VEC; ++k) acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], off);
+            if (sub == 0 && c0 < p.ncols) store_l2<VEC>(p.partials + (long long)warp * p.pstride + c0, acc);
+        }
+        // Publish the partial row, then count this segment in.
+        __threadfence();
+        __syncwarp();
+        unsigned int prev = 0;
+        if (lane == 0) prev = atomicAdd(p.counters + s.w, 1u);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        const int4 L = p.longs[s.w];
+        if (prev + 1 == (unsigned int)L.z) {
+            // Last segment of this row: fixed-order reduction of all partials.
+            __threadfence();
+            for (int pass = 0; pass < npass; ++pass) {
+                const int c0 = pass * CPP + gl * VEC;
+                float acc[VEC];
+#pragma unroll
+                for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
+                if (c0 < p.ncols)
+                    for (int q = L.y + sub; q < L.y + L.z; q += P)
+                        add_l2<VEC>(p.partials + (long long)q * p.pstride + c0, acc);
+#pragma unroll
+                for (int off = G; off < 32; off <<= 1)
+#pragma unroll
+                    for (int k = 0; k < VEC; ++k) acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], off);
+                if (sub == 0 && c0 < p.ncols) store_c<VEC>(p.C + (long long)L.x * p.ldc + c0, acc);
+            }
+            if (lane == 0) p.counters[s.w] = 0u;  // ready for the next launch
+        }
+        return;
+    }
+
+    const int w = warp - p.n_segs;
+    if (w >= p.n_ranges) return;
+    const int2 rg = p.ranges[w];
+    for (int r = rg.x + sub; r < rg.y; r += P) {
+        const int b = __ldg(p.row_ptr + r), e = __ldg(p.row_ptr + r + 1);
+        if (e - b > p.long_thr) continue;  // written by its segments
+        for (int pass = 0; pass < npass; ++pass) {
+            const int c0 = pass * CPP + gl * VEC;
+            if (c0 >= p.ncols) break;
+            float acc[VEC];
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
+            accumulate<T, VEC, U>(p, b, e, 1, c0, acc);
+            store_c<VEC>(p.C + (long long)r * p.ldc + c0, acc);
+        }
+    }
+}
+
+}  // namespace tca

@@ -1,0 +1,260 @@
+// Host preprocessor: splits A into tensor-core windows (dense condensed column
+// tiles) and CUDA-core residue work balanced by nonzeros.
+//
+// Replaces workload_manager (src/our_spmm.cu:353-477), which buckets rows by
+// nnz into 1/2/4/8 warps or several 8-warp blocks and packs them first-fit.
+// Here:
+//   * rows are grouped into windows of R rows; a window whose condensed tiles
+//     move fewer bytes than gathering its rows one nonzero at a time becomes a
+//     tensor-core window (16-bit dtypes only);
+//   * every other row belongs to exactly one contiguous row range, and ranges
+//     carry about the same cost (nnz + per-row overhead) per warp;
+//   * a row longer than twice the per-warp budget is cut into segments whose
+//     partial sums are reduced in a fixed order (deterministic), so one hub row
+//     never serialises a warp.
+// Every nonzero lands in exactly one tile cell, one row range or one segment;
+// tcaspmm_schedule_coverage checks that integer invariant.
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+
+#include "internal.h"
+
+namespace tca {
+
+void residue_shape(int64_t ncols, tcaspmm_dtype dt, bool vector_path, int *G, int *VEC)
+{
+    const int vec = vector_path ? 16 / dtype_size(dt) : 1;
+    const int64_t nvec = (ncols + vec - 1) / vec;
+    int g = 1;
+    while (g < nvec && g < 32) g *= 2;
+    *G = g;
+    *VEC = vec;
+}
+
+static int64_t env_int(const char *name, int64_t dflt)
+{
+    const char *s = std::getenv(name);
+    if (!s || !*s) return dflt;
+    return std::atoll(s);
+}
+
+// Condensed-tile selection for one window: returns the sorted union of the
+// window's columns and whether tiles beat per-nonzero gathers on bytes moved.
+static bool window_prefers_tc(const tcaspmm_csr &A, int64_t r0, int64_t r1, int KT, int R,
+                              int64_t ncols, int elem, std::vector<int32_t> *cols_u, int64_t *nnz_w)
+{
+    cols_u->clear();
+    int64_t nz = 0;
+    for (int64_t r = r0; r < r1; r++) {
+        const int64_t b = A.row_ptr[r], e = A.row_ptr[r + 1];
+        nz += e - b;
+        cols_u->insert(cols_u->end(), A.col_idx + b, A.col_idx + e);
+    }
+    *nnz_w = nz;
+    if (nz == 0) return false;
+    std::sort(cols_u->begin(), cols_u->end());
+    cols_u->erase(std::unique(cols_u->begin(), cols_u->end()), cols_u->end());
+    const int64_t ntiles = ((int64_t)cols_u->size() + KT - 1) / KT;
+    const double row_bytes = (double)ncols * elem;
+    const double tc_bytes = (double)ntiles * KT * (row_bytes + 4) + (double)ntiles * R * KT * elem;
+    const double res_bytes = (double)nz * (row_bytes + 4 + elem);
+    const double density = (double)nz / ((double)ntiles * KT * (r1 - r0));
+    return density >= 1.0 / 64.0 && tc_bytes < 0.8 * res_bytes;
+}
+
+tcaspmm_status build_schedule(const tcaspmm_csr &A, int64_t ncols, tcaspmm_dtype dt,
+                              const ScheduleOptions &opt, Schedule *out)
+{
+    auto t0 = std::chrono::steady_clock::now();
+    Schedule &S = *out;
+    S = Schedule();
+    S.M = A.nrow;
+    S.K = A.ncol;
+    S.nnz = A.nnz;
+    S.ncols = ncols;
+    S.dt = dt;
+    const int elem = dtype_size(dt);
+    const int64_t M = A.nrow;
+
+    // ---- tensor-core windows (16-bit dtypes) ----
+    const int R = 32;
+    S.tc.R = R;
+    S.tc.KT = 16;
+    S.win_shift = 5;
+    const int64_t nwin = (M + R - 1) / R;
+    S.win_tc.assign((size_t)nwin, 0);
+    const bool tc_ok = opt.allow_tc && dt != TCASPMM_F32 && ncols > 0 && env_int("TCASPMM_DISABLE_TC", 0) == 0;
+    if (tc_ok) {
+        std::vector<int32_t> cols_u;
+        for (int64_t w = 0; w < nwin; w++) {
+            const int64_t r0 = w * R, r1 = std::min<int64_t>(M, r0 + R);
+            int64_t nz;
+            if (!window_prefers_tc(A, r0, r1, S.tc.KT, R, ncols, elem, &cols_u, &nz)) continue;
+            S.win_tc[w] = 1;
+            const int KT = S.tc.KT;
+            const int64_t ntiles = ((int64_t)cols_u.size() + KT - 1) / KT;
+            const int64_t t_first = (int64_t)S.tc.tile_cols.size() / KT;
+            S.tc.windows.push_back(Int4{(int32_t)r0, (int32_t)t_first, (int32_t)ntiles, (int32_t)(r1 - r0)});
+            const size_t cbase = S.tc.tile_cols.size();
+            S.tc.tile_cols.resize(cbase + ntiles * KT);
+            for (int64_t q = 0; q < ntiles * KT; q++)
+                S.tc.tile_cols[cbase + q] = q < (int64_t)cols_u.size() ? cols_u[q] : cols_u.back();
+            const size_t vbase = S.tc.tile_vals.size();
+            S.tc.tile_vals.resize(vbase + ntiles * R * KT, 0.0f);
+            for (int64_t r = r0; r < r1; r++) {
+                for (int64_t j = A.row_ptr[r]; j < A.row_ptr[r + 1]; j++) {
+                    const int64_t p = std::lower_bound(cols_u.begin(), cols_u.end(), A.col_idx[j]) - cols_u.begin();
+                    const int64_t t = p / KT, k = p % KT;
+                    S.tc.tile_vals[vbase + (t * R + (r - r0)) * KT + k] = A.val ? A.val[j] : 1.0f;
+                }
+            }
+            S.tc.nnz += nz;
+        }
+    }
+
+    // ---- residue rows ----
+    ResidueSchedule &RS = S.res;
+    residue_shape(ncols, dt, true, &RS.G, &RS.VEC);
+    RS.P = 32 / RS.G;
+    const int P = RS.P;
+    const int64_t BETA = 2;  // per-row cost (row_ptr read, C row write) in nonzero units
+    auto in_tc = [&](int64_t r) { return S.win_tc[r >> S.win_shift] != 0; };
+    int64_t W = 0;
+    for (int64_t r = 0; r < M; r++)
+        if (!in_tc(r)) W += (A.row_ptr[r + 1] - A.row_ptr[r]) + BETA;
+    const int64_t target_warps = (int64_t)opt.num_sms * env_int("TCASPMM_WARPS_PER_SM", 32);
+    int64_t base = W / std::max<int64_t>(1, (int64_t)P * target_warps);
+    base = std::min<int64_t>(std::max<int64_t>(base, env_int("TCASPMM_BUDGET_MIN", 128)),
+                             env_int("TCASPMM_BUDGET_MAX", 1024));
+    const int64_t warp_budget = base * P;  // a warp runs P rows (or P nnz streams) at once
+    RS.long_thr = (int32_t)std::min<int64_t>(INT32_MAX, 2 * base);
+    const int64_t seg_len = warp_budget;
+
+    // Long rows -> segments (issued first so they start early).
+    for (int64_t r = 0; r < M; r++) {
+        if (in_tc(r)) continue;
+        const int64_t b = A.row_ptr[r], e = A.row_ptr[r + 1], L = e - b;
+        if (L <= RS.long_thr) continue;
+        const int64_t nseg = (L + seg_len - 1) / seg_len;
+        const int32_t long_id = (int32_t)RS.longs.size();
+        RS.longs.push_back(Int4{(int32_t)r, (int32_t)RS.segs.size(), (int32_t)nseg, 0});
+        for (int64_t k = 0; k < nseg; k++)
+            RS.segs.push_back(Int4{(int32_t)r, (int32_t)(b + L * k / nseg), (int32_t)(b + L * (k + 1) / nseg), long_id});
+        RS.nnz += L;
+    }
+    // Row ranges: runs of non-tensor-core rows, cut every warp_budget of cost.
+    // Long rows cost 1 inside a range (the warp only reads their length).
+    int64_t start = -1, acc = 0;
+    for (int64_t r = 0; r < M; r++) {
+        if (in_tc(r)) {
+            if (start >= 0) RS.ranges.push_back(Int2{(int32_t)start, (int32_t)r});
+            start = -1;
+            acc = 0;
+            continue;
+        }
+        if (start < 0) start = r;
+        const int64_t L = A.row_ptr[r + 1] - A.row_ptr[r];
+        if (L > RS.long_thr) {
+            acc += 1;
+        } else {
+            acc += L + BETA;
+            RS.nnz += L;
+        }
+        if (acc >= warp_budget) {
+            RS.ranges.push_back(Int2{(int32_t)start, (int32_t)(r + 1)});
+            start = -1;
+            acc = 0;
+        }
+    }
+    if (start >= 0) RS.ranges.push_back(Int2{(int32_t)start, (int32_t)M});
+
+    S.build_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    return TCASPMM_OK;
+}
+
+}  // namespace tca
+
+using namespace tca;
+
+extern "C" tcaspmm_status tcaspmm_schedule_coverage(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt,
+                                                    int32_t *cover, int8_t *kind, tcaspmm_plan_stats *stats)
+{
+    if (!A || !cover || !kind || N < 0 || !dtype_valid(dt))
+        return fail(TCASPMM_ERR_INVALID_ARG, "schedule_coverage: bad arguments");
+    tcaspmm_status s = tcaspmm_csr_validate(A);
+    if (s != TCASPMM_OK) return s;
+    Schedule S;
+    ScheduleOptions opt;
+    s = build_schedule(*A, N, dt, opt, &S);
+    if (s != TCASPMM_OK) return s;
+    std::memset(cover, 0, sizeof(int32_t) * A->nnz);
+    std::memset(kind, 0, (size_t)A->nnz);
+    auto mark = [&](int64_t j, int8_t k) {
+        cover[j]++;
+        kind[j] = k;
+    };
+    // Tile cells: locate every nonzero of a tc window in its tiles and check
+    // the stored column and value; then count nonzero cells (no extras).
+    const int R = S.tc.R, KT = S.tc.KT;
+    int64_t cells = 0;
+    for (const Int4 &w : S.tc.windows) {
+        const int32_t *tc = S.tc.tile_cols.data() + (int64_t)w.y * KT;
+        const float *tv = S.tc.tile_vals.data() + (int64_t)w.y * R * KT;
+        const int64_t ncond = (int64_t)w.z * KT;
+        for (int64_t r = w.x; r < w.x + w.w; r++) {
+            for (int64_t j = A->row_ptr[r]; j < A->row_ptr[r + 1]; j++) {
+                const int32_t c = A->col_idx[j];
+                int64_t p = std::lower_bound(tc, tc + ncond, c) - tc;
+                if (p >= ncond || tc[p] != c) continue;  // not covered: reported by cover[j] == 0
+                const float v = tv[((p / KT) * R + (r - w.x)) * KT + p % KT];
+                if (v != (A->val ? A->val[j] : 1.0f)) continue;
+                mark(j, 3);
+            }
+        }
+        for (int64_t q = 0; q < (int64_t)w.z * R * KT; q++) cells += tv[q] != 0.0f;
+    }
+    int64_t tc_val_nnz = 0;
+    for (int64_t j = 0; j < A->nnz; j++) tc_val_nnz += kind[j] == 3 && (A->val ? A->val[j] : 1.0f) != 0.0f;
+    if (cells != tc_val_nnz)
+        return fail(TCASPMM_ERR_FORMAT, "tiles hold %lld nonzero cells for %lld covered nonzeros",
+                    (long long)cells, (long long)tc_val_nnz);
+    // Residue, walked exactly as the kernel walks it.
+    const ResidueSchedule &RS = S.res;
+    for (const Int2 &rg : RS.ranges) {
+        for (int64_t r = rg.x; r < rg.y; r++) {
+            if (S.win_tc[r >> S.win_shift])
+                return fail(TCASPMM_ERR_FORMAT, "row range holds tensor-core row %lld", (long long)r);
+            const int64_t b = A->row_ptr[r], e = A->row_ptr[r + 1];
+            if (e - b > RS.long_thr) continue;
+            for (int64_t j = b; j < e; j++) mark(j, 1);
+        }
+    }
+    for (const Int4 &g : RS.segs) {
+        const Int4 &L = RS.longs[g.w];
+        if (L.x != g.x || g.y < A->row_ptr[g.x] || g.z > A->row_ptr[g.x + 1] || g.y > g.z)
+            return fail(TCASPMM_ERR_FORMAT, "segment outside its row");
+        for (int64_t j = g.y; j < g.z; j++) mark(j, 2);
+    }
+    if (stats) {
+        std::memset(stats, 0, sizeof(*stats));
+        stats->nrow = A->nrow;
+        stats->ncol = A->ncol;
+        stats->nnz = A->nnz;
+        stats->ncols_total = N;
+        stats->num_shards = 1;
+        stats->window_rows = R;
+        stats->tc_windows = (int64_t)S.tc.windows.size();
+        stats->tc_tiles = (int64_t)S.tc.tile_cols.size() / (KT ? KT : 1);
+        stats->tc_nnz = S.tc.nnz;
+        stats->residue_nnz = RS.nnz;
+        stats->residue_row_warps = (int64_t)RS.ranges.size();
+        stats->residue_segments = (int64_t)RS.segs.size();
+        stats->long_rows = (int64_t)RS.longs.size();
+        stats->preprocess_ms = S.build_ms;
+        stats->algorithmic_bytes = algorithmic_bytes(A->nrow, A->ncol, A->nnz, N, dt);
+    }
+    return TCASPMM_OK;
+}

@@ -1,0 +1,214 @@
+// ./test <matrix.smtx> [-n N] [-d f16|bf16|f32] [-i iters] [-g gpus] [--seed S]
+//
+// Drop-in for the reference driver (src/test.cu:29-88): loads the .smtx file,
+// builds B (K x N, default N = 256 as src/test.cu:47), runs dense cuBLAS
+// GemmEx (the reference's gold), cuSPARSE SpMM and tcaspmm, validates both
+// against the gold with compare_mat's rule (an element fails only if both its
+// absolute and relative error reach 1e-3, src/general.cuh:71-123), and prints
+// the reference's three timing lines followed by one JSON line.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "tcaspmm.h"
+#include "tcaspmm_baselines.h"
+
+#define CK(x)                                                                                        \
+    do {                                                                                             \
+        cudaError_t e_ = (x);                                                                        \
+        if (e_ != cudaSuccess) {                                                                     \
+            std::fprintf(stderr, "CUDA error at [%s : %d] %d %s\n", __FILE__, __LINE__, (int)e_,     \
+                         cudaGetErrorString(e_));                                                    \
+            std::exit(EXIT_FAILURE);                                                                 \
+        }                                                                                            \
+    } while (0)
+#define TK(x)                                                                                        \
+    do {                                                                                             \
+        tcaspmm_status s_ = (x);                                                                     \
+        if (s_ != TCASPMM_OK) {                                                                      \
+            std::fprintf(stderr, "tcaspmm error at [%s : %d] %s: %s\n", __FILE__, __LINE__,          \
+                         tcaspmm_status_string(s_), tcaspmm_last_error());                           \
+            std::exit(EXIT_FAILURE);                                                                 \
+        }                                                                                            \
+    } while (0)
+
+static bool compare_mat(const float *gold, const float *cmp, int64_t n, float tol)
+{
+    int64_t bad = 0;
+    for (int64_t i = 0; i < n; i++) {
+        const float d = std::fabs(gold[i] - cmp[i]);
+        const float rel = std::fabs(d / gold[i]);
+        if (rel >= tol && d >= tol) {
+            if (bad < 10)
+                std::printf("Discrepancy occured in %lldth element :: %f vs %f ...abs_disc : %f, rel_disc : %f %%\n",
+                            (long long)i, gold[i], cmp[i], d, rel * 100.0);
+            if (++bad >= 10) return false;
+        }
+    }
+    return bad == 0;
+}
+
+int main(int argc, char **argv)
+{
+    const char *path = nullptr;
+    int64_t N = 256;
+    int iters = 10, gpus = 1;
+    uint64_t seed = 0;
+    tcaspmm_dtype dt = TCASPMM_F16;
+    for (int i = 1; i < argc; i++) {
+        std::string a = argv[i];
+        auto next = [&]() -> const char * {
+            if (i + 1 >= argc) {
+                std::fprintf(stderr, "missing value for %s\n", a.c_str());
+                std::exit(EXIT_FAILURE);
+            }
+            return argv[++i];
+        };
+        if (a == "-n") N = std::atoll(next());
+        else if (a == "-i") iters = std::atoi(next());
+        else if (a == "-g") gpus = std::atoi(next());
+        else if (a == "--seed") seed = std::strtoull(next(), nullptr, 10);
+        else if (a == "-d") {
+            std::string d = next();
+            dt = d == "f32" ? TCASPMM_F32 : d == "bf16" ? TCASPMM_BF16 : TCASPMM_F16;
+        } else path = argv[i];
+    }
+    if (!path) {
+        std::puts("Usage : ./test {matrix.smtx} [-n N] [-d f16|bf16|f32] [-i iters] [-g gpus] [--seed S]");
+        return EXIT_FAILURE;
+    }
+    tcaspmm_csr A;
+    TK(tcaspmm_smtx_read(path, &A));
+    const int64_t M = A.nrow, K = A.ncol, nnz = A.nnz;
+    const int elem = dt == TCASPMM_F32 ? 4 : 2;
+    std::printf("Input file - %s\n", path);
+
+    std::vector<char> hB((size_t)(K * N * elem) + 16);
+    TK(tcaspmm_gen_dense(K, N, seed, dt, hB.data()));
+    std::vector<float> Cgold((size_t)(M * N), 0.0f), Cmp((size_t)(M * N), 0.0f);
+
+    // Round A's values to dt on the host (the device copy the plan makes).
+    std::vector<float> aval(nnz, 1.0f);
+    if (A.val) std::copy(A.val, A.val + nnz, aval.begin());
+
+    double e_gemm = -1.0, e_cusparse = -1.0, e_our = -1.0;
+    void *dB = nullptr;
+    float *dC = nullptr;
+    CK(cudaMalloc(&dB, K * N * elem + 16));
+    CK(cudaMalloc((void **)&dC, M * N * 4 + 16));
+    CK(cudaMemcpy(dB, hB.data(), K * N * elem, cudaMemcpyHostToDevice));
+
+    // Dense cuBLAS gold, when the dense A fits comfortably.
+    bool have_gold = false;
+    if (M * K * elem <= ((int64_t)8 << 30)) {
+        std::vector<char> dense((size_t)(M * K * elem), 0);
+        // The plan rounds values the same way; reuse its device copy through a
+        // 1-GPU plan to get identical bits for the dense matrix.
+        tcaspmm_plan *p1 = nullptr;
+        TK(tcaspmm_plan_create(&A, N, dt, 1, nullptr, &p1));
+        const int32_t *drp, *dcol;
+        const void *dval;
+        TK(tcaspmm_plan_device_csr(p1, 0, &drp, &dcol, &dval));
+        std::vector<char> hv((size_t)nnz * elem + 16);
+        if (nnz) CK(cudaMemcpy(hv.data(), dval, nnz * elem, cudaMemcpyDeviceToHost));
+        for (int64_t r = 0; r < M; r++)
+            for (int64_t j = A.row_ptr[r]; j < A.row_ptr[r + 1]; j++)
+                std::memcpy(&dense[(r * K + A.col_idx[j]) * elem], &hv[j * elem], elem);
+        void *dA = nullptr;
+        CK(cudaMalloc(&dA, M * K * elem + 16));
+        CK(cudaMemcpy(dA, dense.data(), M * K * elem, cudaMemcpyHostToDevice));
+        if (tcaspmm_cublas_gemm(dA, dB, dC, M, N, K, dt, 5, iters, nullptr, &e_gemm) == TCASPMM_OK) {
+            CK(cudaMemcpy(Cgold.data(), dC, M * N * 4, cudaMemcpyDeviceToHost));
+            have_gold = true;
+        }
+        CK(cudaFree(dA));
+        // cuSPARSE on the plan's device CSR.
+        CK(cudaMemset(dC, 0, M * N * 4));
+        if (tcaspmm_cusparse_spmm(drp, dcol, dval, M, K, nnz, dB, N, dC, N, N, dt, 10, iters, nullptr, &e_cusparse) ==
+            TCASPMM_OK) {
+            CK(cudaMemcpy(Cmp.data(), dC, M * N * 4, cudaMemcpyDeviceToHost));
+            if (have_gold && !compare_mat(Cgold.data(), Cmp.data(), M * N, 1e-3f))
+                std::printf("\033[35mvalidation failed (Cusparse)\033[0m\n");
+        }
+        tcaspmm_plan_destroy(p1);
+    }
+
+    // tcaspmm over `gpus` devices: column blocks of B and C per device.
+    tcaspmm_plan *plan = nullptr;
+    TK(tcaspmm_plan_create(&A, N, dt, gpus, nullptr, &plan));
+    tcaspmm_plan_stats st;
+    TK(tcaspmm_plan_get_stats(plan, &st));
+    std::printf("preprocess %fms taken\n", st.preprocess_ms);
+    std::vector<void *> sB(gpus);
+    std::vector<float *> sC(gpus);
+    std::vector<int64_t> ldb(gpus), ldc(gpus), cb(gpus), cc(gpus);
+    std::vector<void *> streams(gpus, nullptr);
+    std::vector<cudaEvent_t> ev0(gpus), ev1(gpus);
+    for (int g = 0; g < gpus; g++) {
+        int dev;
+        TK(tcaspmm_plan_shard(plan, g, &dev, &cb[g], &cc[g]));
+        CK(cudaSetDevice(dev));
+        ldb[g] = ldc[g] = std::max<int64_t>(cc[g], 1);
+        CK(cudaMalloc(&sB[g], K * ldb[g] * elem + 16));
+        CK(cudaMalloc((void **)&sC[g], M * ldc[g] * 4 + 16));
+        if (cc[g] && K)
+            CK(cudaMemcpy2D(sB[g], ldb[g] * elem, hB.data() + cb[g] * elem, N * elem, cc[g] * elem, K,
+                            cudaMemcpyHostToDevice));
+        CK(cudaEventCreate(&ev0[g]));
+        CK(cudaEventCreate(&ev1[g]));
+    }
+    for (int i = 0; i < 5; i++) TK(tcaspmm_execute(plan, sB.data(), ldb.data(), sC.data(), ldc.data(), streams.data()));
+    for (int g = 0; g < gpus; g++) {
+        int dev;
+        tcaspmm_plan_shard(plan, g, &dev, nullptr, nullptr);
+        CK(cudaSetDevice(dev));
+        CK(cudaDeviceSynchronize());
+        CK(cudaEventRecord(ev0[g], 0));
+    }
+    for (int i = 0; i < iters; i++)
+        TK(tcaspmm_execute(plan, sB.data(), ldb.data(), sC.data(), ldc.data(), streams.data()));
+    float worst = 0.0f;
+    for (int g = 0; g < gpus; g++) {
+        int dev;
+        tcaspmm_plan_shard(plan, g, &dev, nullptr, nullptr);
+        CK(cudaSetDevice(dev));
+        CK(cudaEventRecord(ev1[g], 0));
+        CK(cudaEventSynchronize(ev1[g]));
+        float ms;
+        CK(cudaEventElapsedTime(&ms, ev0[g], ev1[g]));
+        worst = std::max(worst, ms);
+        if (cc[g] && M)
+            CK(cudaMemcpy2D(Cmp.data() + cb[g], N * 4, sC[g], ldc[g] * 4, cc[g] * 4, M, cudaMemcpyDeviceToHost));
+    }
+    TK(tcaspmm_plan_sync_check(plan));
+    e_our = iters ? worst / iters : 0.0;
+    if (have_gold && !compare_mat(Cgold.data(), Cmp.data(), M * N, 1e-3f))
+        std::printf("\033[35mvalidation failed (Our, balanced)\033[0m\n");
+
+    std::printf("GemmEx : \033[36m[%lf] ms\033[0m\n", e_gemm);
+    std::printf("cuSPARSE: \033[36m[%lf] ms\033[0m \n", e_cusparse);
+    std::printf("our: \033[36m[%lf] ms\033[0m \n", e_our);
+    const double flops = 2.0 * (double)nnz * (double)N;
+    std::printf("{\"matrix\": \"%s\", \"M\": %lld, \"K\": %lld, \"N\": %lld, \"nnz\": %lld, \"dtype\": \"%s\", "
+                "\"gpus\": %d, \"ms\": {\"ours\": %.6f, \"cusparse\": %.6f, \"gemm_cublas\": %.6f}, "
+                "\"gflops\": %.3f, \"algorithmic_bytes\": %lld, \"tc_windows\": %lld, \"residue_nnz\": %lld}\n",
+                path, (long long)M, (long long)K, (long long)N, (long long)nnz,
+                dt == TCASPMM_F32 ? "f32" : dt == TCASPMM_F16 ? "f16" : "bf16", gpus, e_our, e_cusparse, e_gemm,
+                e_our > 0 ? flops / (e_our * 1e6) : 0.0, (long long)st.algorithmic_bytes, (long long)st.tc_windows,
+                (long long)st.residue_nnz);
+    for (int g = 0; g < gpus; g++) {
+        cudaFree(sB[g]);
+        cudaFree(sC[g]);
+    }
+    tcaspmm_plan_destroy(plan);
+    cudaFree(dB);
+    cudaFree(dC);
+    tcaspmm_csr_free(&A);
+    return 0;
+}

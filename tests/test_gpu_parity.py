@@ -1,0 +1,184 @@
+"""CUDA path vs the CPU oracle, through the C-ABI library.
+
+Tolerances (north star): rel-L2 <= 1e-5 against the fp64 CSR oracle on the
+same rounded inputs for the CUDA-core path, <= 5e-3 for the tensor-core path
+(fp16/bf16 windows).  Integer-valued inputs are compared bit-exactly.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import spmm_b200 as T
+
+pytestmark = pytest.mark.gpu
+
+TOL_CORE = 1e-5
+TOL_TC = 5e-3
+
+
+def _torch_dt(dt):
+    return {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[dt]
+
+
+def _round(x: np.ndarray, dt: str) -> np.ndarray:
+    """Values as the device sees them (rounded to dt), widened to float32."""
+    return torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(_torch_dt(dt)).float().numpy()
+
+
+def run(A: T.CSR, B: np.ndarray, dt: str, ldb_pad: int = 0, ldc_pad: int = 0, stream=None):
+    """C = A @ B on cuda:0 through tcaspmm_execute1; B given in fp32, rounded to dt."""
+    K, N = B.shape
+    Bt = torch.from_numpy(np.ascontiguousarray(B, np.float32)).to(_torch_dt(dt))
+    Bd = torch.zeros((K, N + ldb_pad), dtype=_torch_dt(dt), device="cuda")
+    Bd[:, :N] = Bt.cuda()
+    Cd = torch.full((A.nrow, N + ldc_pad), float("nan"), dtype=torch.float32, device="cuda")
+    with T.Plan(A, N, dt) as p:
+        p.execute1(Bd[:, :N], Cd[:, :N], stream=stream or torch.cuda.current_stream())
+        p.sync_check()
+        st = p.stats
+    torch.cuda.synchronize()
+    if ldc_pad:
+        assert torch.isnan(Cd[:, N:]).all(), "wrote outside the C view"
+    return Cd[:, :N].cpu().numpy(), st
+
+
+def reference(A: T.CSR, B: np.ndarray, dt: str) -> np.ndarray:
+    return oracle.spmm_f64(A.row_ptr, A.col, _round(A.values(), dt), _round(B, dt))
+
+
+def check(A, N, dt, seed=0, tol=None, **kw):
+    B = T.gen_dense(A.ncol, N, seed, "f32")
+    out, st = run(A, B, dt, **kw)
+    ref = reference(A, B, dt)
+    if tol is None:
+        tol = TOL_TC if st["tc_nnz"] > 0 else TOL_CORE
+    err = oracle.rel_l2(out, ref)
+    assert err <= tol, (err, st)
+    assert np.isfinite(out).all()
+    return out, st
+
+
+def test_bundled_integer_known_answer_bit_exact(bundled):
+    A = T.CSR(int(bundled["M"]), int(bundled["K"]), bundled["row_ptr"], bundled["col"], None)
+    out, _ = run(A, bundled["B_int"].astype(np.float32), "f16")
+    np.testing.assert_array_equal(out, bundled["C_int"])
+
+
+def test_bundled_random_matches_reference_gemm(bundled):
+    A = T.CSR(int(bundled["M"]), int(bundled["K"]), bundled["row_ptr"], bundled["col"], None)
+    out, _ = run(A, bundled["B_rand"].astype(np.float32), "f16")
+    assert oracle.rel_l2(out, bundled["C_rand"]) < 1e-6
+
+
+def test_small_reference_cases(small_cases):
+    for c in small_cases:
+        A = T.CSR(c["M"], c["K"], c["row_ptr"], c["col"], c["val"].astype(np.float32))
+        out, _ = run(A, c["B"].astype(np.float32), "f16")
+        assert oracle.rel_l2(out, c["C"]) < 1e-6, c["dense"].shape
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("N", [256, 1, 7, 24, 64, 129, 512])
+def test_c1_ffn_uniform(dt, N):
+    check(T.gen_uniform(2048, 512, 0.3, 0), N, dt)
+
+
+@pytest.mark.parametrize("shape", [(512, 2048), (2048, 2048), (4096, 1024)])
+@pytest.mark.parametrize("sparsity", [0.5, 0.9, 0.98])
+@pytest.mark.parametrize("kind", ["uniform", "magnitude"])
+def test_c2_sweep(shape, sparsity, kind):
+    M, K = shape
+    A = T.gen_uniform(M, K, 1 - sparsity, 1) if kind == "uniform" else T.gen_magnitude(M, K, sparsity, 1)
+    for dt, N in (("f16", 128), ("f32", 64)):
+        check(A, N, dt)
+
+
+@pytest.mark.parametrize("dt,N", [("f32", 128), ("f16", 128), ("f32", 16), ("f16", 32)])
+def test_gcn_rmat_small(dt, N):
+    check(T.gen_rmat(16, 500000, kind="gcn", seed=2), N, dt)
+
+
+@pytest.mark.parametrize("dt,N", [("f16", 64), ("f32", 64), ("bf16", 8)])
+def test_skew_hub_rows_use_segments(dt, N):
+    A = T.gen_skew(300000, 16, 50000, 3.0, seed=4)
+    _, st = check(A, N, dt)
+    assert st["long_rows"] >= 16 and st["residue_segments"] > 16
+
+
+def test_sage_mean_small():
+    check(T.gen_rmat(15, 400000, kind="sage", seed=3), 256, "f16")
+
+
+def test_unaligned_leading_dimensions_take_scalar_path():
+    A = T.gen_uniform(300, 200, 0.1, 5)
+    check(A, 37, "f16", ldb_pad=3, ldc_pad=1)
+    check(A, 37, "f32", ldb_pad=1, ldc_pad=3)
+
+
+def test_padded_views_do_not_write_outside_c():
+    A = T.gen_uniform(100, 64, 0.2, 6)
+    check(A, 64, "f16", ldb_pad=8, ldc_pad=4)
+
+
+def test_edge_shapes():
+    empty = T.CSR(50, 20, np.zeros(51, np.int64), np.zeros(0, np.int32), None)
+    out, _ = run(empty, np.ones((20, 16), np.float32), "f32")
+    assert np.all(out == 0)
+    one = T.CSR(3, 4, np.array([0, 0, 1, 1]), np.array([2]), np.array([-2.5], np.float32))
+    B = np.arange(4 * 8, dtype=np.float32).reshape(4, 8)
+    out, _ = run(one, B, "f32")
+    np.testing.assert_array_equal(out, np.vstack([np.zeros(8), -2.5 * B[2], np.zeros(8)]))
+    out, _ = run(T.CSR(0, 5, np.zeros(1, np.int64), np.zeros(0, np.int32), None), np.ones((5, 8), np.float32), "f16")
+    assert out.shape == (0, 8)
+    check(T.gen_uniform(1, 1, 1.0, 0), 1, "f32")
+
+
+def test_single_dense_row_and_column():
+    row = T.gen_uniform(1, 50000, 1.0, 7)       # one hub row: segments + fix-up
+    _, st = check(row, 64, "f32")
+    assert st["residue_segments"] > 1
+    colm = T.gen_uniform(20000, 1, 1.0, 8)      # every row has one nonzero
+    check(colm, 256, "f16")
+
+
+def test_deterministic_across_runs():
+    A = T.gen_skew(100000, 8, 40000, 3.0, seed=9)
+    B = T.gen_dense(A.ncol, 64, 1, "f32")
+    a, _ = run(A, B, "f32")
+    b, _ = run(A, B, "f32")
+    np.testing.assert_array_equal(a, b)
+
+
+def test_runs_on_a_side_stream():
+    s = torch.cuda.Stream()
+    A = T.gen_uniform(1000, 300, 0.05, 10)
+    check(A, 128, "f32", stream=s)
+
+
+def test_reference_entry_point_bit_exact(bundled):
+    M, K, N = int(bundled["M"]), int(bundled["K"]), int(bundled["N"])
+    Cout = np.zeros(M * N, np.float32)
+    ms = T.our_spmm_balanced(bundled["row_ptr"].astype(np.int32), bundled["col"], bundled["val_bits"].view(np.float16),
+                             bundled["B_int"], Cout, M, N, K, 10)
+    assert ms > 0
+    np.testing.assert_array_equal(Cout.reshape(M, N), bundled["C_int"])
+
+
+def test_multi_gpu_column_shards():
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("one GPU")
+    A = T.gen_rmat(14, 100000, kind="gcn", seed=1)
+    N, dt = 128, "f32"
+    B = T.gen_dense(A.ncol, N, 3, "f32")
+    with T.Plan(A, N, dt, num_gpus=2) as p:
+        Bs, Cs = [], []
+        for s in range(2):
+            dev, b, c = p.shard(s)
+            Bs.append(torch.from_numpy(B[:, b:b + c].copy()).to(f"cuda:{dev}"))
+            Cs.append(torch.empty((A.nrow, c), device=f"cuda:{dev}"))
+        p.execute(Bs, Cs, streams=[torch.cuda.current_stream(f"cuda:{p.shard(s)[0]}") for s in range(2)])
+        p.sync_check()
+        out = np.hstack([c.cpu().numpy() for c in Cs])
+    assert oracle.rel_l2(out, reference(A, B, dt)) <= TOL_CORE
