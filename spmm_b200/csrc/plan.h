@@ -20,6 +20,11 @@ struct Shard {
     int32_t *row_ptr = nullptr;
     int32_t *col = nullptr;
     void *val = nullptr;
+    // L2 policy of the residue kernel (0 default, 1 stream evict-first,
+    // 2 also hot/cold B rows) and, for 2, columns with the hot bit set.
+    int hint = 1;
+    int32_t *col_hot = nullptr;
+    int64_t hot_cols = 0;
 
     // Residue schedule + scratch.
     Int2 *ranges = nullptr;
@@ -33,9 +38,12 @@ struct Shard {
 
     // Tensor-core windows.
     int n_windows = 0;
-    Int4 *tc_windows = nullptr;  // {first row, first tile, tiles, rows}
-    int32_t *tc_cols = nullptr;  // KT B-row indices per tile
-    void *tc_vals = nullptr;     // R x KT values per tile, shared-memory image
+    int num_sms = 148;
+    Int4 *tc_windows = nullptr;   // {first row, first tile, tiles, rows}
+    int32_t *tc_order = nullptr;  // windows by decreasing tile count
+    int32_t *tc_cols = nullptr;   // KT B-row indices per tile
+    void *tc_vals = nullptr;      // R x KT values per tile, shared-memory image
+    Int2 *tc_fallback = nullptr;  // one row range per window (unaligned B: CUDA cores)
 
     int *err = nullptr;  // device error word (bounded waits that ran out)
 };
@@ -48,7 +56,9 @@ bool tc_supported();
 tcaspmm_status tc_upload(const tcaspmm_csr &A, tcaspmm_dtype dt, Shard *sh);
 tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int64_t ldb, float *dC, int64_t ldc,
                          cudaStream_t st);
+// CUDA-core residue kernel over the shard's row ranges and segments, or, with
+// `ranges` given, over those ranges only (whole rows, no segments).
 tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB, int64_t ldb, float *dC,
-                              int64_t ldc, cudaStream_t st);
+                              int64_t ldc, cudaStream_t st, const Int2 *ranges = nullptr, int n_ranges = 0);
 
 }  // namespace tca

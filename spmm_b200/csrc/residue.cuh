@@ -19,6 +19,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cstdint>
+#include <cstring>
 #include <type_traits>
 
 namespace tca {
@@ -43,6 +44,55 @@ struct ResidueParams {
     int long_thr;
 };
 
+// L2 policies.  HINT 0: default caching.  HINT 1: the CSR stream (offsets,
+// columns, values) is read L1::no_allocate + L2 evict_first, so it does not
+// displace B rows.  HINT 2: as 1, and each column index carries a hot bit
+// (bit 30, set at plan time for the highest-degree columns whose B rows fit
+// in part of L2): hot B rows are read evict_last, cold ones evict_first.
+constexpr int32_t HOT_BIT = 1 << 30;
+
+struct Policies {
+    uint64_t first, last;
+};
+
+__device__ __forceinline__ Policies make_policies()
+{
+    Policies p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p.first));
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p.last));
+    return p;
+}
+
+template <int HINT>
+__device__ __forceinline__ int ld_stream_i32(const int32_t *ptr, uint64_t pol)
+{
+    if constexpr (HINT == 0) {
+        return __ldg(ptr);
+    } else {
+        int v;
+        asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.b32 %0, [%1], %2;" : "=r"(v) : "l"(ptr), "l"(pol));
+        return v;
+    }
+}
+
+template <int HINT, typename T>
+__device__ __forceinline__ T ld_stream_val(const T *ptr, uint64_t pol)
+{
+    if constexpr (HINT == 0) {
+        return __ldg(ptr);
+    } else if constexpr (sizeof(T) == 4) {
+        float v;
+        asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(v) : "l"(ptr), "l"(pol));
+        return v;
+    } else {
+        unsigned short v;
+        asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.b16 %0, [%1], %2;" : "=h"(v) : "l"(ptr), "l"(pol));
+        T t;
+        memcpy(&t, &v, 2);
+        return t;
+    }
+}
+
 template <typename T> __device__ __forceinline__ float to_f(T x);
 template <> __device__ __forceinline__ float to_f<float>(float x) { return x; }
 template <> __device__ __forceinline__ float to_f<__half>(__half x) { return __half2float(x); }
@@ -52,13 +102,19 @@ template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 x
 template <typename T, int VEC> struct Raw { uint4 u; };
 template <typename T> struct Raw<T, 1> { T s; };
 
-template <typename T, int VEC>
-__device__ __forceinline__ void load_raw(const T *p, Raw<T, VEC> &r)
+template <typename T, int VEC, int HINT>
+__device__ __forceinline__ void load_raw(const T *p, Raw<T, VEC> &r, uint64_t pol)
 {
-    if constexpr (VEC == 1)
-        r.s = __ldg(p);
-    else
-        r.u = __ldg(reinterpret_cast<const uint4 *>(p));
+    if constexpr (VEC == 1 || HINT < 2) {
+        if constexpr (VEC == 1)
+            r.s = __ldg(p);
+        else
+            r.u = __ldg(reinterpret_cast<const uint4 *>(p));
+    } else {
+        asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+                     : "=r"(r.u.x), "=r"(r.u.y), "=r"(r.u.z), "=r"(r.u.w)
+                     : "l"(p), "l"(pol));
+    }
 }
 
 template <typename T, int VEC>
@@ -144,9 +200,9 @@ __device__ __forceinline__ void add_l2(const float *c, float (&a)[VEC])
 // acc += sum_{j = b, b+stride, ... < e} val[j] * B[col[j]][c0 .. c0+VEC).
 // The U column indices of a step are read first, then U independent B loads
 // are issued, then the FMAs, so each lane keeps U loads in flight.
-template <typename T, int VEC, int U>
+template <typename T, int VEC, int U, int HINT>
 __device__ __forceinline__ void accumulate(const ResidueParams &p, int b, int e, int stride, int c0,
-                                           float (&acc)[VEC])
+                                           float (&acc)[VEC], const Policies &pol)
 {
     const T *__restrict__ B = static_cast<const T *>(p.B) + c0;
     const T *__restrict__ val = static_cast<const T *>(p.val);
@@ -157,25 +213,29 @@ __device__ __forceinline__ void accumulate(const ResidueParams &p, int b, int e,
         for (int u = 0; u < U; ++u) {
             const int jj = j + u * stride;
             const bool ok = jj < e;
-            cc[u] = ok ? __ldg(p.col + jj) : -1;
-            vv[u] = ok ? to_f<T>(__ldg(val + jj)) : 0.0f;
+            cc[u] = ok ? ld_stream_i32<HINT>(p.col + jj, pol.first) : -1;
+            vv[u] = ok ? to_f<T>(ld_stream_val<HINT>(val + jj, pol.first)) : 0.0f;
         }
         Raw<T, VEC> rb[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            if (cc[u] >= 0)
-                load_raw<T, VEC>(B + (long long)cc[u] * p.ldb, rb[u]);
-            else
+            if (cc[u] >= 0) {
+                const int c = HINT == 2 ? (cc[u] & ~HOT_BIT) : cc[u];
+                const uint64_t bp = (HINT == 2 && (cc[u] & HOT_BIT)) ? pol.last : pol.first;
+                load_raw<T, VEC, HINT>(B + (long long)c * p.ldb, rb[u], bp);
+            } else {
                 zero_raw<T, VEC>(rb[u]);
+            }
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) fma_raw<T, VEC>(vv[u], rb[u], acc);
     }
 }
 
-template <typename T, int VEC, int G, int U>
+template <typename T, int VEC, int G, int U, int HINT>
 __global__ void __launch_bounds__(256) residue_kernel(const ResidueParams p)
 {
+    const Policies pol = HINT ? make_policies() : Policies{0, 0};
     constexpr int P = 32 / G;
     constexpr int CPP = G * VEC;  // columns per pass
     const int lane = threadIdx.x & 31;
@@ -190,7 +250,7 @@ __global__ void __launch_bounds__(256) residue_kernel(const ResidueParams p)
             float acc[VEC];
 #pragma unroll
             for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
-            if (c0 < p.ncols) accumulate<T, VEC, U>(p, s.y + sub, s.z, P, c0, acc);
+            if (c0 < p.ncols) accumulate<T, VEC, U, HINT>(p, s.y + sub, s.z, P, c0, acc, pol);
 #pragma unroll
             for (int off = G; off < 32; off <<= 1)
 #pragma unroll
@@ -230,7 +290,8 @@ __global__ void __launch_bounds__(256) residue_kernel(const ResidueParams p)
     if (w >= p.n_ranges) return;
     const int2 rg = p.ranges[w];
     for (int r = rg.x + sub; r < rg.y; r += P) {
-        const int b = __ldg(p.row_ptr + r), e = __ldg(p.row_ptr + r + 1);
+        const int b = ld_stream_i32<HINT>(p.row_ptr + r, pol.first);
+        const int e = ld_stream_i32<HINT>(p.row_ptr + r + 1, pol.first);
         if (e - b > p.long_thr) continue;  // written by its segments
         for (int pass = 0; pass < npass; ++pass) {
             const int c0 = pass * CPP + gl * VEC;
@@ -238,7 +299,7 @@ __global__ void __launch_bounds__(256) residue_kernel(const ResidueParams p)
             float acc[VEC];
 #pragma unroll
             for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
-            accumulate<T, VEC, U>(p, b, e, 1, c0, acc);
+            accumulate<T, VEC, U, HINT>(p, b, e, 1, c0, acc, pol);
             store_c<VEC>(p.C + (long long)r * p.ldc + c0, acc);
         }
     }

@@ -86,7 +86,8 @@ tcaspmm_status build_schedule(const tcaspmm_csr &A, int64_t ncols, tcaspmm_dtype
     S.win_shift = 5;
     const int64_t nwin = (M + R - 1) / R;
     S.win_tc.assign((size_t)nwin, 0);
-    const bool tc_ok = opt.allow_tc && dt != TCASPMM_F32 && ncols > 0 && env_int("TCASPMM_DISABLE_TC", 0) == 0;
+    const bool tc_ok = opt.allow_tc && dt != TCASPMM_F32 && ncols > 0 && ncols % 8 == 0 &&
+                       env_int("TCASPMM_DISABLE_TC", 0) == 0;
     if (tc_ok) {
         std::vector<int32_t> cols_u;
         for (int64_t w = 0; w < nwin; w++) {

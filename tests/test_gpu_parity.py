@@ -182,3 +182,39 @@ def test_multi_gpu_column_shards():
         p.sync_check()
         out = np.hstack([c.cpu().numpy() for c in Cs])
     assert oracle.rel_l2(out, reference(A, B, dt)) <= TOL_CORE
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("N", [256, 128, 64, 8, 200])
+def test_tensor_core_windows(dt, N):
+    """C1 at 70% sparsity: every window is dense enough for the tcgen05 tiles."""
+    _, st = check(T.gen_uniform(2048, 512, 0.3, 0), N, dt)
+    assert st["tc_windows"] == 64 and st["tc_nnz"] == st["nnz"]
+
+
+def test_tensor_core_windows_mixed_with_residue():
+    """Magnitude pruning with skewed row scales: dense windows on tcgen05, the rest on CUDA cores."""
+    A = T.gen_magnitude(4096, 1024, 0.9, 3)
+    _, st = check(A, 128, "f16")
+    assert st["tc_windows"] > 0 and st["residue_nnz"] > 0
+
+
+def test_tensor_core_partial_window_and_block():
+    """M not a multiple of 32 rows, N not a multiple of 128 columns."""
+    _, st = check(T.gen_uniform(1000, 300, 0.4, 11), 72, "f16")
+    assert st["tc_windows"] > 0
+
+
+def test_tensor_core_unaligned_b_falls_back_to_cuda_cores():
+    _, st = check(T.gen_uniform(256, 256, 0.4, 12), 64, "f16", ldb_pad=3)
+    assert st["tc_windows"] > 0
+
+
+def test_tensor_core_integer_values_bit_exact():
+    """Small integers: every product and partial sum is exact in fp32, on tcgen05 too."""
+    A = T.gen_uniform(512, 256, 0.5, 13)
+    A = T.CSR(A.nrow, A.ncol, A.row_ptr, A.col, np.round(A.val * 2).astype(np.float32))
+    B = np.round(T.gen_dense(256, 128, 2, "f32") * 3).astype(np.float32)
+    out, st = run(A, B, "f16")
+    assert st["tc_windows"] > 0
+    np.testing.assert_array_equal(out, reference(A, B, "f16").astype(np.float32))
