@@ -64,9 +64,9 @@ struct TileSchedule {
     int64_t nnz = 0;
 };
 
-// CUDA-core residue work.  Row ranges are runs of rows outside tensor-core
-// windows.  A row in a range is handled whole by that range's warp when its
-// length is <= long_thr, else it is split into segments.
+// CUDA-core residue work.  Row ranges are runs of rows that are neither in
+// tensor-core windows nor longer than long_thr; each is handled whole by its
+// range's warp.  Rows longer than long_thr are split into segments.
 struct ResidueSchedule {
     int G = 32;                      // lanes per row slice
     int VEC = 4;                     // elements per lane load

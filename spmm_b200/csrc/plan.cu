@@ -123,7 +123,7 @@ tcaspmm_status build_shard(const tcaspmm_csr &A, tcaspmm_dtype dt, int device, i
         }
     }
     // L2 policy and the hot-column copy of the column indices (policy 2).
-    sh->hint = (int)env_int("TCASPMM_L2_HINT", 2);
+    sh->hint = (int)env_int("TCASPMM_L2_HINT", 0);
     if (sh->hint < 0 || sh->hint > 2) sh->hint = 1;
     if (sh->hint == 2 && (A.ncol >= (int64_t)1 << 30 || A.nnz == 0)) sh->hint = 1;
     if (sh->hint == 2) {
@@ -252,7 +252,6 @@ tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB,
     p.partials = sh.partials;
     p.pstride = sh.pstride;
     p.counters = sh.counters;
-    p.long_thr = whole_rows ? INT_MAX : sh.long_thr;
     if (dt == TCASPMM_F32)
         launch_res_t<float>(vec, sh.hint, G, p, total, st);
     else if (dt == TCASPMM_F16)

@@ -57,7 +57,7 @@ tcaspmm_status tc_upload(const tcaspmm_csr &A, tcaspmm_dtype dt, Shard *sh);
 tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int64_t ldb, float *dC, int64_t ldc,
                          cudaStream_t st);
 // CUDA-core residue kernel over the shard's row ranges and segments, or, with
-// `ranges` given, over those ranges only (whole rows, no segments).
+// `ranges` given, over those ranges only (whole rows of any length, no segments).
 tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB, int64_t ldb, float *dC,
                               int64_t ldc, cudaStream_t st, const Int2 *ranges = nullptr, int n_ranges = 0);
 

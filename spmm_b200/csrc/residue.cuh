@@ -7,9 +7,10 @@
 //   * a lane group of G lanes (power of two) covers G*VEC columns of one B row
 //     with 16-byte loads (VEC = 4 fp32 or 8 fp16/bf16); a warp holds P = 32/G
 //     groups, and columns beyond G*VEC are covered by extra passes;
-//   * row warps: each group walks its rows of a contiguous row range (group s
-//     takes rows s, s+P, ...) with U independent B loads in flight per lane and
-//     writes each finished C row with streaming 16-byte stores;
+//   * row warps: each group streams the nonzeros of its contiguous share of a
+//     row range in chunks of U (U independent B loads in flight per lane,
+//     however short the rows) and writes each finished C row with streaming
+//     16-byte stores as the stream passes the row's end;
 //   * segment warps: the P groups split one segment of a long row, reduce with
 //     __shfl_xor_sync, and store a partial row; the warp that completes a long
 //     row's last segment (atomic counter) sums all its partials in segment
@@ -41,7 +42,6 @@ struct ResidueParams {
     float *partials;                 // n_segs x pstride
     int pstride;
     unsigned int *counters;          // one per long row, zero between launches
-    int long_thr;
 };
 
 // L2 policies.  HINT 0: default caching.  HINT 1: the CSR stream (offsets,
@@ -232,8 +232,77 @@ __device__ __forceinline__ void accumulate(const ResidueParams &p, int b, int e,
     }
 }
 
+// First row r in [lo, hi] with row_ptr[r] >= target.
+__device__ __forceinline__ int first_row_at(const int32_t *row_ptr, int lo, int hi, int target)
+{
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (__ldg(row_ptr + mid) < target)
+            lo = mid + 1;
+        else
+            hi = mid;
+    }
+    return lo;
+}
+
+// C rows [r_lo, r_hi), columns c0 .. c0+VEC: one pass over their nonzeros in
+// chunks of U (loads first, then FMAs), writing each row as the stream leaves it.
+template <typename T, int VEC, int U, int HINT>
+__device__ __forceinline__ void stream_rows(const ResidueParams &p, int r_lo, int r_hi, int c0, const Policies &pol)
+{
+    if (r_lo >= r_hi) return;
+    const T *__restrict__ B = static_cast<const T *>(p.B) + c0;
+    const T *__restrict__ val = static_cast<const T *>(p.val);
+    float *__restrict__ C = p.C + c0;
+    int r = r_lo;
+    int e = ld_stream_i32<HINT>(p.row_ptr + r + 1, pol.first);  // end of row r
+    const int jend = ld_stream_i32<HINT>(p.row_ptr + r_hi, pol.first);
+    float acc[VEC];
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
+    for (int j = ld_stream_i32<HINT>(p.row_ptr + r_lo, pol.first); j < jend; j += U) {
+        int cc[U];
+        float vv[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const bool ok = j + u < jend;
+            cc[u] = ok ? ld_stream_i32<HINT>(p.col + j + u, pol.first) : 0;
+            vv[u] = ok ? to_f<T>(ld_stream_val<HINT>(val + j + u, pol.first)) : 0.0f;
+        }
+        Raw<T, VEC> rb[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int c = HINT == 2 ? (cc[u] & ~HOT_BIT) : cc[u];
+            const uint64_t bp = (HINT == 2 && (cc[u] & HOT_BIT)) ? pol.last : pol.first;
+            if (j + u < jend)
+                load_raw<T, VEC, HINT>(B + (long long)c * p.ldb, rb[u], bp);
+            else
+                zero_raw<T, VEC>(rb[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            if (j + u < jend) {
+                while (j + u >= e) {  // the stream left row r: write it
+                    store_c<VEC>(C + (long long)r * p.ldc, acc);
+#pragma unroll
+                    for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
+                    ++r;
+                    e = ld_stream_i32<HINT>(p.row_ptr + r + 1, pol.first);
+                }
+                fma_raw<T, VEC>(vv[u], rb[u], acc);
+            }
+        }
+    }
+    // Rows left: the one in progress, then any trailing empty rows.
+    for (; r < r_hi; ++r) {
+        store_c<VEC>(C + (long long)r * p.ldc, acc);
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
+    }
+}
+
 template <typename T, int VEC, int G, int U, int HINT>
-__global__ void __launch_bounds__(256) residue_kernel(const ResidueParams p)
+__global__ void __launch_bounds__(256, sizeof(T) == 4 ? 4 : 3) residue_kernel(const ResidueParams p)
 {
     const Policies pol = HINT ? make_policies() : Policies{0, 0};
     constexpr int P = 32 / G;
@@ -288,20 +357,24 @@ __global__ void __launch_bounds__(256) residue_kernel(const ResidueParams p)
 
     const int w = warp - p.n_segs;
     if (w >= p.n_ranges) return;
+    // Row range: contiguous rows, none of them long.  Group `sub` streams the
+    // nonzeros of its contiguous share of the rows, U loads in flight whatever
+    // the row lengths, and flushes each C row when the stream passes its end
+    // (empty rows are written as zeros).
     const int2 rg = p.ranges[w];
-    for (int r = rg.x + sub; r < rg.y; r += P) {
-        const int b = ld_stream_i32<HINT>(p.row_ptr + r, pol.first);
-        const int e = ld_stream_i32<HINT>(p.row_ptr + r + 1, pol.first);
-        if (e - b > p.long_thr) continue;  // written by its segments
-        for (int pass = 0; pass < npass; ++pass) {
-            const int c0 = pass * CPP + gl * VEC;
-            if (c0 >= p.ncols) break;
-            float acc[VEC];
-#pragma unroll
-            for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
-            accumulate<T, VEC, U, HINT>(p, b, e, 1, c0, acc, pol);
-            store_c<VEC>(p.C + (long long)r * p.ldc + c0, acc);
-        }
+    int r_lo = rg.x, r_hi = rg.y;
+    if constexpr (P > 1) {
+        // Split the range between the P groups by nonzeros (binary search on
+        // the row offsets); each group gets a contiguous run of rows.
+        const int jb = __ldg(p.row_ptr + rg.x), je = __ldg(p.row_ptr + rg.y);
+        r_lo = sub == 0 ? rg.x : first_row_at(p.row_ptr, rg.x, rg.y, jb + (int)((long long)(je - jb) * sub / P));
+        r_hi = sub == P - 1 ? rg.y
+                            : first_row_at(p.row_ptr, rg.x, rg.y, jb + (int)((long long)(je - jb) * (sub + 1) / P));
+    }
+    for (int pass = 0; pass < npass; ++pass) {
+        const int c0 = pass * CPP + gl * VEC;
+        if (c0 >= p.ncols) break;
+        stream_rows<T, VEC, U, HINT>(p, r_lo, r_hi, c0, pol);
     }
 }
 

@@ -62,7 +62,9 @@ static bool window_prefers_tc(const tcaspmm_csr &A, int64_t r0, int64_t r1, int 
     const double tc_bytes = (double)ntiles * KT * (row_bytes + 4) + (double)ntiles * R * KT * elem;
     const double res_bytes = (double)nz * (row_bytes + 4 + elem);
     const double density = (double)nz / ((double)ntiles * KT * (r1 - r0));
-    return density >= 1.0 / 64.0 && tc_bytes < 0.8 * res_bytes;
+    // A window is one serial chain of tiles on one CTA: cap its length so a hub
+    // window never becomes the critical path, and require real density.
+    return ntiles <= 256 && density >= 1.0 / 8.0 && tc_bytes < 0.8 * res_bytes;
 }
 
 tcaspmm_status build_schedule(const tcaspmm_csr &A, int64_t ncols, tcaspmm_dtype dt,
@@ -146,24 +148,20 @@ tcaspmm_status build_schedule(const tcaspmm_csr &A, int64_t ncols, tcaspmm_dtype
             RS.segs.push_back(Int4{(int32_t)r, (int32_t)(b + L * k / nseg), (int32_t)(b + L * (k + 1) / nseg), long_id});
         RS.nnz += L;
     }
-    // Row ranges: runs of non-tensor-core rows, cut every warp_budget of cost.
-    // Long rows cost 1 inside a range (the warp only reads their length).
+    // Row ranges: runs of rows that are neither tensor-core rows nor long rows,
+    // cut every warp_budget of cost.
     int64_t start = -1, acc = 0;
     for (int64_t r = 0; r < M; r++) {
-        if (in_tc(r)) {
+        const int64_t L = A.row_ptr[r + 1] - A.row_ptr[r];
+        if (in_tc(r) || L > RS.long_thr) {
             if (start >= 0) RS.ranges.push_back(Int2{(int32_t)start, (int32_t)r});
             start = -1;
             acc = 0;
             continue;
         }
         if (start < 0) start = r;
-        const int64_t L = A.row_ptr[r + 1] - A.row_ptr[r];
-        if (L > RS.long_thr) {
-            acc += 1;
-        } else {
-            acc += L + BETA;
-            RS.nnz += L;
-        }
+        acc += L + BETA;
+        RS.nnz += L;
         if (acc >= warp_budget) {
             RS.ranges.push_back(Int2{(int32_t)start, (int32_t)(r + 1)});
             start = -1;
@@ -228,9 +226,7 @@ extern "C" tcaspmm_status tcaspmm_schedule_coverage(const tcaspmm_csr *A, int64_
         for (int64_t r = rg.x; r < rg.y; r++) {
             if (S.win_tc[r >> S.win_shift])
                 return fail(TCASPMM_ERR_FORMAT, "row range holds tensor-core row %lld", (long long)r);
-            const int64_t b = A->row_ptr[r], e = A->row_ptr[r + 1];
-            if (e - b > RS.long_thr) continue;
-            for (int64_t j = b; j < e; j++) mark(j, 1);
+            for (int64_t j = A->row_ptr[r]; j < A->row_ptr[r + 1]; j++) mark(j, 1);
         }
     }
     for (const Int4 &g : RS.segs) {

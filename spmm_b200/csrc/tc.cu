@@ -22,7 +22,7 @@
 // Warp roles (288 threads): warps 0-3 epilogue (tcgen05.ld of TMEM lanes
 // 32w..32w+31 -> coalesced fp32 C rows), warp 4 TMEM allocation + MMA issue
 // (one thread), warps 5-8 producers (cp.async 16-byte gathers of B rows and
-// value tiles into a 6-stage mbarrier ring).  Two TMEM accumulators let the
+// value tiles into a 7-stage mbarrier ring; B-row indices staged in smem).  Two TMEM accumulators let the
 // epilogue of one unit overlap the MMAs of the next.
 //
 // Every mbarrier wait is bounded: on time-out the kernel records a code in the
@@ -46,7 +46,8 @@ namespace {
 constexpr int R = 32;            // window rows = MMA N
 constexpr int KT = 16;           // condensed columns per tile = MMA K (16-bit inputs)
 constexpr int MB = 128;          // output columns per unit = MMA M
-constexpr int STAGES = 6;
+constexpr int STAGES = 7;
+constexpr int IDX_TILES = 32;           // tile column indices staged per producer warp per refill
 constexpr int PANEL_BYTES = MB * KT * 2;  // 4096
 constexpr int VAL_BYTES = R * KT * 2;     // 1024
 constexpr int STAGE_BYTES = PANEL_BYTES + VAL_BYTES;
@@ -184,7 +185,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_kernel(const TcParams p)
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte aligned stage ring, then barriers.
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t *bars = (uint64_t *)(smem + STAGES * STAGE_BYTES);
+    int32_t *idxbuf = (int32_t *)(smem + STAGES * STAGE_BYTES);  // [4 warps][IDX_TILES][KT]
+    uint64_t *bars = (uint64_t *)(smem + STAGES * STAGE_BYTES + 4 * IDX_TILES * KT * 4);
     uint64_t *full = bars;                 // [STAGES] producers -> MMA
     uint64_t *empty = bars + STAGES;       // [STAGES] MMA -> producers
     uint64_t *accf = bars + 2 * STAGES;    // [2] MMA -> epilogue
@@ -223,10 +225,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_kernel(const TcParams p)
 
     if (warp >= 5) {
         // ------------------------------ producers ------------------------------
+        // Each producer warp stages the B-row indices of up to IDX_TILES tiles in
+        // its own shared-memory slice with one cooperative load, so no cp.async
+        // waits on a dependent load.  Only warp-level syncs are used, and every
+        // abort decision is warp-uniform, so a time-out cannot strand a barrier.
         const int pt = tid - 160;       // 0..127
         const int pw = pt >> 5;         // producer warp 0..3: column chunks 4pw..4pw+3
         const int kr = lane & 7;        // row within a core matrix
         const int cc = pw * 4 + (lane >> 3);
+        int32_t *widx = idxbuf + pw * IDX_TILES * KT;
         const char *Bb = (const char *)p.B;
         uint32_t g = 0;
         bool ok = true;
@@ -234,24 +241,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_kernel(const TcParams p)
             const int4 w = p.windows[p.order[u / p.nfb]];
             const int f = (u % p.nfb) * MB + cc * 8;  // first of this thread's 8 columns
             const bool fvalid = f < p.ncols;
-            for (int t = 0; t < w.z; ++t, ++g) {
-                const int s = g % STAGES;
-                if (!wait_bounded(smem_u32(&empty[s]), ((g / STAGES) & 1) ^ 1, abort_flag, p.err, 1)) {
-                    ok = false;
-                    break;
-                }
-                const long long tile = (long long)w.y + t;
-                const uint32_t panel = smem_u32(smem + s * STAGE_BYTES);
+            for (int t0 = 0; ok && t0 < w.z; t0 += IDX_TILES) {
+                const int nt = min(IDX_TILES, w.z - t0);
+                __syncwarp();  // previous indices consumed
+                for (int q = lane; q < nt * KT; q += 32) widx[q] = __ldg(p.tile_cols + ((long long)w.y + t0) * KT + q);
+                __syncwarp();  // indices visible to the warp
+                for (int t = 0; t < nt; ++t, ++g) {
+                    const int s = g % STAGES;
+                    ok = __all_sync(0xffffffffu,
+                                    wait_bounded(smem_u32(&empty[s]), ((g / STAGES) & 1) ^ 1, abort_flag, p.err, 1));
+                    if (!ok) break;
+                    const long long tile = (long long)w.y + t0 + t;
+                    const uint32_t panel = smem_u32(smem + s * STAGE_BYTES);
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    const int kk = i * 8 + kr;
-                    const int brow = __ldg(p.tile_cols + tile * KT + kk);
-                    const char *src = fvalid ? Bb + ((long long)brow * p.ldb + f) * 2 : Bb;
-                    cp_async_16(panel + cc * 256 + i * 128 + kr * 16, src, fvalid ? 16u : 0u);
+                    for (int i = 0; i < 2; ++i) {
+                        const int brow = widx[t * KT + i * 8 + kr];
+                        const char *src = fvalid ? Bb + ((long long)brow * p.ldb + f) * 2 : Bb;
+                        cp_async_16(panel + cc * 256 + i * 128 + kr * 16, src, fvalid ? 16u : 0u);
+                    }
+                    if (pt < VAL_BYTES / 16)
+                        cp_async_16(panel + PANEL_BYTES + pt * 16, p.tile_vals + tile * (R * KT) + pt * 8, 16u);
+                    cp_async_arrive_noinc(smem_u32(&full[s]));
                 }
-                if (pt < VAL_BYTES / 16)
-                    cp_async_16(panel + PANEL_BYTES + pt * 16, p.tile_vals + tile * (R * KT) + pt * 8, 16u);
-                cp_async_arrive_noinc(smem_u32(&full[s]));
             }
         }
         asm volatile("cp.async.wait_all;" ::: "memory");
@@ -296,7 +307,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_kernel(const TcParams p)
         for (int u = blockIdx.x; u < p.n_units; u += gridDim.x, ++i) {
             const int4 w = p.windows[p.order[u / p.nfb]];
             const uint32_t a = i & 1;
-            if (!wait_bounded(smem_u32(&accf[a]), (i >> 1) & 1, abort_flag, p.err, 4)) break;
+            if (!__all_sync(0xffffffffu, wait_bounded(smem_u32(&accf[a]), (i >> 1) & 1, abort_flag, p.err, 4))) break;
             tc_fence_after();
             float v[32];
             tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + a * R, v);
@@ -320,7 +331,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_kernel(const TcParams p)
     }
 }
 
-constexpr size_t kSmemBytes = 1024 + STAGES * STAGE_BYTES + 256;  // < 48 KB: no opt-in needed
+constexpr size_t kSmemBytes = 1024 + STAGES * STAGE_BYTES + 4 * IDX_TILES * KT * 4 + 256;  // < 48 KB
 
 template <typename X>
 tcaspmm_status upload_vec(Shard *sh, X **dst, const std::vector<X> &v, const char *what)

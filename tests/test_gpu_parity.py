@@ -192,11 +192,16 @@ def test_tensor_core_windows(dt, N):
     assert st["tc_windows"] == 64 and st["tc_nnz"] == st["nnz"]
 
 
+def _vstack(a: T.CSR, b: T.CSR) -> T.CSR:
+    return T.CSR(a.nrow + b.nrow, a.ncol, np.concatenate([a.row_ptr, b.row_ptr[1:] + a.nnz]),
+                 np.concatenate([a.col, b.col]), np.concatenate([a.values(), b.values()]))
+
+
 def test_tensor_core_windows_mixed_with_residue():
-    """Magnitude pruning with skewed row scales: dense windows on tcgen05, the rest on CUDA cores."""
-    A = T.gen_magnitude(4096, 1024, 0.9, 3)
+    """Dense rows on tcgen05 next to sparse rows on CUDA cores in one matrix."""
+    A = _vstack(T.gen_uniform(512, 1024, 0.5, 3), T.gen_uniform(3000, 1024, 0.005, 4))
     _, st = check(A, 128, "f16")
-    assert st["tc_windows"] > 0 and st["residue_nnz"] > 0
+    assert st["tc_windows"] == 16 and st["residue_nnz"] > 0
 
 
 def test_tensor_core_partial_window_and_block():
