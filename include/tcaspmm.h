@@ -207,6 +207,26 @@ void our_spmm_balanced(tcaspmm_ref_csr *A_csr, uint16_t *B, float *C, int M, int
 tcaspmm_status tcaspmm_our_spmm_balanced(const tcaspmm_ref_csr *A_csr, const uint16_t *B, float *C,
                                          int M, int N, int K, int n_iter, double *elapsed);
 
+/* ------------------------------------------------ no-allocation entry point
+ * No counterpart in the reference: an addition for callers that must not
+ * allocate device memory at the moment they multiply (a plugin inside a host
+ * framework that owns every device allocation, a latency-critical loop where an
+ * allocation could block or fragment a memory pool, a caller with a fixed
+ * memory budget).  C = A * B with A in CSR already in the caller's device memory
+ * (int32 offsets [M+1], int32 columns [nnz], values [nnz] in dt), B (K x N, ld
+ * ldb, dt) and fp32 C (M x N, ld ldc) in device memory, launched on `stream`.
+ * It calls no cudaMalloc / cudaFree and no allocating library routine: its only
+ * scratch is a fixed 16 MiB array inside the library image, which every GPU
+ * that loads the library holds until the process exits.  Limit: two partial
+ * rows of N floats (N rounded up to 4) must fit in that array, so N <= 2097152;
+ * larger N returns TCASPMM_ERR_UNSUPPORTED.  All calls share the array: calls
+ * whose kernels overlap on the GPU race and must be serialised by the caller.
+ * The first call on each device looks up the array's device address with that
+ * device current; make that first call before any stream capture. */
+tcaspmm_status tcaspmm_spmm_csr_noalloc(const int32_t *d_row_ptr, const int32_t *d_col, const void *d_val,
+                                        int64_t M, int64_t K, int64_t nnz, const void *dB, int64_t ldb, float *dC,
+                                        int64_t ldc, int64_t N, tcaspmm_dtype dt, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
