@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(256) noalloc_chunks(const NoallocParams p)
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
                 if (j + u < j1)
-                    load_raw<T, VEC, 0>(B + (long long)cc[u] * p.ldb, rb[u], 0);
+                    load_raw<T, VEC>(B + (long long)cc[u] * p.ldb, rb[u]);
                 else
                     zero_raw<T, VEC>(rb[u]);
             }

@@ -30,12 +30,6 @@ tcaspmm_status cuda_fail(cudaError_t e, const char *what)
 
 namespace {
 
-int64_t env_int(const char *name, int64_t dflt)
-{
-    const char *v = std::getenv(name);
-    return (v && *v) ? std::atoll(v) : dflt;
-}
-
 struct DeviceGuard {
     int prev = -1;
     explicit DeviceGuard(int dev)
@@ -122,32 +116,6 @@ tcaspmm_status build_shard(const tcaspmm_csr &A, tcaspmm_dtype dt, int device, i
             sh->val = d;
         }
     }
-    // L2 policy and the hot-column copy of the column indices (policy 2).
-    sh->hint = (int)env_int("TCASPMM_L2_HINT", 0);
-    if (sh->hint < 0 || sh->hint > 2) sh->hint = 1;
-    if (sh->hint == 2 && (A.ncol >= (int64_t)1 << 30 || A.nnz == 0)) sh->hint = 1;
-    if (sh->hint == 2) {
-        // Hot columns: highest degree first, as many B rows as fit in
-        // TCASPMM_HOT_MB of L2 (default 64 MB), degree >= 2.
-        std::vector<int32_t> deg((size_t)A.ncol, 0);
-        for (int64_t j = 0; j < A.nnz; j++) deg[A.col_idx[j]]++;
-        const int64_t row_bytes = std::max<int64_t>(1, ncols * dtype_size(dt));
-        const int64_t budget = env_int("TCASPMM_HOT_MB", 64) * (1 << 20) / row_bytes;
-        std::vector<int32_t> order((size_t)A.ncol);
-        for (int64_t c = 0; c < A.ncol; c++) order[c] = (int32_t)c;
-        const int64_t take = std::min<int64_t>(budget, A.ncol);
-        std::nth_element(order.begin(), order.begin() + (take ? take - 1 : 0), order.end(),
-                         [&](int32_t a, int32_t b) { return deg[a] > deg[b]; });
-        std::vector<uint8_t> hot((size_t)A.ncol, 0);
-        for (int64_t q = 0; q < take; q++)
-            if (deg[order[q]] >= 2) {
-                hot[order[q]] = 1;
-                sh->hot_cols++;
-            }
-        std::vector<int32_t> ch((size_t)A.nnz);
-        for (int64_t j = 0; j < A.nnz; j++) ch[j] = A.col_idx[j] | (hot[A.col_idx[j]] ? HOT_BIT : 0);
-        if ((s = upload(*sh, &sh->col_hot, ch.data(), ch.size(), "hot column indices")) != TCASPMM_OK) return s;
-    }
     // Residue schedule and its scratch (partials + counters).
     const ResidueSchedule &RS = S.res;
     static_assert(sizeof(Int2) == sizeof(int2) && sizeof(Int4) == sizeof(int4), "layout");
@@ -174,44 +142,33 @@ tcaspmm_status build_shard(const tcaspmm_csr &A, tcaspmm_dtype dt, int device, i
     return TCASPMM_OK;
 }
 
-template <typename T, int VEC, int G, int HINT>
+template <typename T, int VEC, int G>
 void launch_res(const ResidueParams &p, int total_warps, cudaStream_t st)
 {
     const int blocks = (total_warps + 7) / 8;
-    residue_kernel<T, VEC, G, 8, HINT><<<blocks, 256, 0, st>>>(p);
-}
-
-template <typename T, int VEC, int HINT>
-void launch_res_g(int G, const ResidueParams &p, int total_warps, cudaStream_t st)
-{
-    switch (G) {
-    case 1: launch_res<T, VEC, 1, HINT>(p, total_warps, st); break;
-    case 2: launch_res<T, VEC, 2, HINT>(p, total_warps, st); break;
-    case 4: launch_res<T, VEC, 4, HINT>(p, total_warps, st); break;
-    case 8: launch_res<T, VEC, 8, HINT>(p, total_warps, st); break;
-    case 16: launch_res<T, VEC, 16, HINT>(p, total_warps, st); break;
-    default: launch_res<T, VEC, 32, HINT>(p, total_warps, st); break;
-    }
+    residue_kernel<T, VEC, G, 8><<<blocks, 256, 0, st>>>(p);
 }
 
 template <typename T, int VEC>
-void launch_res_h(int hint, int G, const ResidueParams &p, int total_warps, cudaStream_t st)
+void launch_res_g(int G, const ResidueParams &p, int total_warps, cudaStream_t st)
 {
-    if (hint == 2)
-        launch_res_g<T, VEC, 2>(G, p, total_warps, st);
-    else if (hint == 1)
-        launch_res_g<T, VEC, 1>(G, p, total_warps, st);
-    else
-        launch_res_g<T, VEC, 0>(G, p, total_warps, st);
+    switch (G) {
+    case 1: launch_res<T, VEC, 1>(p, total_warps, st); break;
+    case 2: launch_res<T, VEC, 2>(p, total_warps, st); break;
+    case 4: launch_res<T, VEC, 4>(p, total_warps, st); break;
+    case 8: launch_res<T, VEC, 8>(p, total_warps, st); break;
+    case 16: launch_res<T, VEC, 16>(p, total_warps, st); break;
+    default: launch_res<T, VEC, 32>(p, total_warps, st); break;
+    }
 }
 
 template <typename T>
-void launch_res_t(bool vec, int hint, int G, const ResidueParams &p, int total_warps, cudaStream_t st)
+void launch_res_t(bool vec, int G, const ResidueParams &p, int total_warps, cudaStream_t st)
 {
     if (vec)
-        launch_res_h<T, 16 / sizeof(T)>(hint, G, p, total_warps, st);
+        launch_res_g<T, 16 / sizeof(T)>(G, p, total_warps, st);
     else
-        launch_res_h<T, 1>(hint, G, p, total_warps, st);
+        launch_res_g<T, 1>(G, p, total_warps, st);
 }
 
 }  // namespace
@@ -237,7 +194,7 @@ tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB,
     // same ranges with its own G (more passes), which stays correct.
     ResidueParams p;
     p.row_ptr = sh.row_ptr;
-    p.col = sh.hint == 2 ? sh.col_hot : sh.col;
+    p.col = sh.col;
     p.val = sh.val;
     p.B = dB;
     p.ldb = ldb;
@@ -253,11 +210,11 @@ tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB,
     p.pstride = sh.pstride;
     p.counters = sh.counters;
     if (dt == TCASPMM_F32)
-        launch_res_t<float>(vec, sh.hint, G, p, total, st);
+        launch_res_t<float>(vec, G, p, total, st);
     else if (dt == TCASPMM_F16)
-        launch_res_t<__half>(vec, sh.hint, G, p, total, st);
+        launch_res_t<__half>(vec, G, p, total, st);
     else
-        launch_res_t<__nv_bfloat16>(vec, sh.hint, G, p, total, st);
+        launch_res_t<__nv_bfloat16>(vec, G, p, total, st);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "residue kernel launch");
     return TCASPMM_OK;

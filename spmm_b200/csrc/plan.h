@@ -20,11 +20,6 @@ struct Shard {
     int32_t *row_ptr = nullptr;
     int32_t *col = nullptr;
     void *val = nullptr;
-    // L2 policy of the residue kernel (0 default, 1 stream evict-first,
-    // 2 also hot/cold B rows) and, for 2, columns with the hot bit set.
-    int hint = 1;
-    int32_t *col_hot = nullptr;
-    int64_t hot_cols = 0;
 
     // Residue schedule + scratch.
     Int2 *ranges = nullptr;

@@ -20,7 +20,6 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cstdint>
-#include <cstring>
 #include <type_traits>
 
 namespace tca {
@@ -44,55 +43,6 @@ struct ResidueParams {
     unsigned int *counters;          // one per long row, zero between launches
 };
 
-// L2 policies.  HINT 0: default caching.  HINT 1: the CSR stream (offsets,
-// columns, values) is read L1::no_allocate + L2 evict_first, so it does not
-// displace B rows.  HINT 2: as 1, and each column index carries a hot bit
-// (bit 30, set at plan time for the highest-degree columns whose B rows fit
-// in part of L2): hot B rows are read evict_last, cold ones evict_first.
-constexpr int32_t HOT_BIT = 1 << 30;
-
-struct Policies {
-    uint64_t first, last;
-};
-
-__device__ __forceinline__ Policies make_policies()
-{
-    Policies p;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p.first));
-    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p.last));
-    return p;
-}
-
-template <int HINT>
-__device__ __forceinline__ int ld_stream_i32(const int32_t *ptr, uint64_t pol)
-{
-    if constexpr (HINT == 0) {
-        return __ldg(ptr);
-    } else {
-        int v;
-        asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.b32 %0, [%1], %2;" : "=r"(v) : "l"(ptr), "l"(pol));
-        return v;
-    }
-}
-
-template <int HINT, typename T>
-__device__ __forceinline__ T ld_stream_val(const T *ptr, uint64_t pol)
-{
-    if constexpr (HINT == 0) {
-        return __ldg(ptr);
-    } else if constexpr (sizeof(T) == 4) {
-        float v;
-        asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(v) : "l"(ptr), "l"(pol));
-        return v;
-    } else {
-        unsigned short v;
-        asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.b16 %0, [%1], %2;" : "=h"(v) : "l"(ptr), "l"(pol));
-        T t;
-        memcpy(&t, &v, 2);
-        return t;
-    }
-}
-
 template <typename T> __device__ __forceinline__ float to_f(T x);
 template <> __device__ __forceinline__ float to_f<float>(float x) { return x; }
 template <> __device__ __forceinline__ float to_f<__half>(__half x) { return __half2float(x); }
@@ -102,19 +52,13 @@ template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 x
 template <typename T, int VEC> struct Raw { uint4 u; };
 template <typename T> struct Raw<T, 1> { T s; };
 
-template <typename T, int VEC, int HINT>
-__device__ __forceinline__ void load_raw(const T *p, Raw<T, VEC> &r, uint64_t pol)
+template <typename T, int VEC>
+__device__ __forceinline__ void load_raw(const T *p, Raw<T, VEC> &r)
 {
-    if constexpr (VEC == 1 || HINT < 2) {
-        if constexpr (VEC == 1)
-            r.s = __ldg(p);
-        else
-            r.u = __ldg(reinterpret_cast<const uint4 *>(p));
-    } else {
-        asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
-                     : "=r"(r.u.x), "=r"(r.u.y), "=r"(r.u.z), "=r"(r.u.w)
-                     : "l"(p), "l"(pol));
-    }
+    if constexpr (VEC == 1)
+        r.s = __ldg(p);
+    else
+        r.u = __ldg(reinterpret_cast<const uint4 *>(p));
 }
 
 template <typename T, int VEC>
@@ -197,12 +141,11 @@ __device__ __forceinline__ void add_l2(const float *c, float (&a)[VEC])
     }
 }
 
-// acc += sum_{j = b, b+stride, ... < e} val[j] * B[col[j]][c0 .. c0+VEC).
-// The U column indices of a step are read first, then U independent B loads
-// are issued, then the FMAs, so each lane keeps U loads in flight.
-template <typename T, int VEC, int U, int HINT>
-__device__ __forceinline__ void accumulate(const ResidueParams &p, int b, int e, int stride, int c0,
-                                           float (&acc)[VEC], const Policies &pol)
+// acc += sum_{j = b, b+stride, ... < e} val[j] * B[col[j]][c0 .. c0+VEC): U
+// indices, then U independent B loads, then the FMAs (no prefetch; few registers).
+template <typename T, int VEC, int U>
+__device__ __forceinline__ void accumulate_simple(const ResidueParams &p, int b, int e, int stride, int c0,
+                                                  float (&acc)[VEC])
 {
     const T *__restrict__ B = static_cast<const T *>(p.B) + c0;
     const T *__restrict__ val = static_cast<const T *>(p.val);
@@ -213,22 +156,77 @@ __device__ __forceinline__ void accumulate(const ResidueParams &p, int b, int e,
         for (int u = 0; u < U; ++u) {
             const int jj = j + u * stride;
             const bool ok = jj < e;
-            cc[u] = ok ? ld_stream_i32<HINT>(p.col + jj, pol.first) : -1;
-            vv[u] = ok ? to_f<T>(ld_stream_val<HINT>(val + jj, pol.first)) : 0.0f;
+            cc[u] = ok ? __ldg(p.col + jj) : -1;
+            vv[u] = ok ? to_f<T>(__ldg(val + jj)) : 0.0f;
         }
         Raw<T, VEC> rb[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            if (cc[u] >= 0) {
-                const int c = HINT == 2 ? (cc[u] & ~HOT_BIT) : cc[u];
-                const uint64_t bp = (HINT == 2 && (cc[u] & HOT_BIT)) ? pol.last : pol.first;
-                load_raw<T, VEC, HINT>(B + (long long)c * p.ldb, rb[u], bp);
-            } else {
+            if (cc[u] >= 0)
+                load_raw<T, VEC>(B + (long long)cc[u] * p.ldb, rb[u]);
+            else
                 zero_raw<T, VEC>(rb[u]);
-            }
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) fma_raw<T, VEC>(vv[u], rb[u], acc);
+    }
+}
+
+// Lean nonzero stream over C rows [r_lo, r_hi) for one lane: full chunks of U
+// run without predicates (U indices, U B loads, U FMAs with a row-end check),
+// the remainder one nonzero at a time; each row is written when the stream
+// passes its end, trailing empty rows too.
+template <typename T, int VEC, int U>
+__device__ __forceinline__ void stream_lean(const ResidueParams &p, int r_lo, int r_hi, int c0)
+{
+    if (r_lo >= r_hi) return;
+    const T *__restrict__ B = static_cast<const T *>(p.B) + c0;
+    const T *__restrict__ val = static_cast<const T *>(p.val);
+    float *__restrict__ C = p.C + c0;
+    int r = r_lo;
+    int e = __ldg(p.row_ptr + r + 1);
+    int j = __ldg(p.row_ptr + r_lo);
+    const int jend = __ldg(p.row_ptr + r_hi);
+    float acc[VEC];
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
+    auto pass_row_ends = [&](int jj) {
+        while (jj >= e) {
+            store_c<VEC>(C + (long long)r * p.ldc, acc);
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
+            ++r;
+            e = __ldg(p.row_ptr + r + 1);
+        }
+    };
+    for (; j + U <= jend; j += U) {
+        int cc[U];
+        float vv[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            cc[u] = __ldg(p.col + j + u);
+            vv[u] = to_f<T>(__ldg(val + j + u));
+        }
+        Raw<T, VEC> rb[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) load_raw<T, VEC>(B + (long long)cc[u] * p.ldb, rb[u]);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            pass_row_ends(j + u);
+            fma_raw<T, VEC>(vv[u], rb[u], acc);
+        }
+    }
+    for (; j < jend; ++j) {
+        Raw<T, VEC> rb;
+        const float v = to_f<T>(__ldg(val + j));
+        load_raw<T, VEC>(B + (long long)__ldg(p.col + j) * p.ldb, rb);
+        pass_row_ends(j);
+        fma_raw<T, VEC>(v, rb, acc);
+    }
+    for (; r < r_hi; ++r) {
+        store_c<VEC>(C + (long long)r * p.ldc, acc);
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
     }
 }
 
@@ -245,66 +243,12 @@ __device__ __forceinline__ int first_row_at(const int32_t *row_ptr, int lo, int 
     return lo;
 }
 
-// C rows [r_lo, r_hi), columns c0 .. c0+VEC: one pass over their nonzeros in
-// chunks of U (loads first, then FMAs), writing each row as the stream leaves it.
-template <typename T, int VEC, int U, int HINT>
-__device__ __forceinline__ void stream_rows(const ResidueParams &p, int r_lo, int r_hi, int c0, const Policies &pol)
+// 256 threads, register budget for 4 resident blocks per SM (64 registers):
+// measured faster than 40 registers / 6 blocks and than 80 / 3 on GCN, SAGE and
+// the skew config.
+template <typename T, int VEC, int G, int U>
+__global__ void __launch_bounds__(256, 4) residue_kernel(const ResidueParams p)
 {
-    if (r_lo >= r_hi) return;
-    const T *__restrict__ B = static_cast<const T *>(p.B) + c0;
-    const T *__restrict__ val = static_cast<const T *>(p.val);
-    float *__restrict__ C = p.C + c0;
-    int r = r_lo;
-    int e = ld_stream_i32<HINT>(p.row_ptr + r + 1, pol.first);  // end of row r
-    const int jend = ld_stream_i32<HINT>(p.row_ptr + r_hi, pol.first);
-    float acc[VEC];
-#pragma unroll
-    for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
-    for (int j = ld_stream_i32<HINT>(p.row_ptr + r_lo, pol.first); j < jend; j += U) {
-        int cc[U];
-        float vv[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const bool ok = j + u < jend;
-            cc[u] = ok ? ld_stream_i32<HINT>(p.col + j + u, pol.first) : 0;
-            vv[u] = ok ? to_f<T>(ld_stream_val<HINT>(val + j + u, pol.first)) : 0.0f;
-        }
-        Raw<T, VEC> rb[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int c = HINT == 2 ? (cc[u] & ~HOT_BIT) : cc[u];
-            const uint64_t bp = (HINT == 2 && (cc[u] & HOT_BIT)) ? pol.last : pol.first;
-            if (j + u < jend)
-                load_raw<T, VEC, HINT>(B + (long long)c * p.ldb, rb[u], bp);
-            else
-                zero_raw<T, VEC>(rb[u]);
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            if (j + u < jend) {
-                while (j + u >= e) {  // the stream left row r: write it
-                    store_c<VEC>(C + (long long)r * p.ldc, acc);
-#pragma unroll
-                    for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
-                    ++r;
-                    e = ld_stream_i32<HINT>(p.row_ptr + r + 1, pol.first);
-                }
-                fma_raw<T, VEC>(vv[u], rb[u], acc);
-            }
-        }
-    }
-    // Rows left: the one in progress, then any trailing empty rows.
-    for (; r < r_hi; ++r) {
-        store_c<VEC>(C + (long long)r * p.ldc, acc);
-#pragma unroll
-        for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
-    }
-}
-
-template <typename T, int VEC, int G, int U, int HINT>
-__global__ void __launch_bounds__(256, sizeof(T) == 4 ? 4 : 3) residue_kernel(const ResidueParams p)
-{
-    const Policies pol = HINT ? make_policies() : Policies{0, 0};
     constexpr int P = 32 / G;
     constexpr int CPP = G * VEC;  // columns per pass
     const int lane = threadIdx.x & 31;
@@ -314,12 +258,14 @@ __global__ void __launch_bounds__(256, sizeof(T) == 4 ? 4 : 3) residue_kernel(co
 
     if (warp < p.n_segs) {
         const int4 s = p.segs[warp];
+        // Group `sub` takes nonzeros s.y + sub, s.y + sub + P, ...; the groups
+        // are then reduced with shuffles in a fixed order.
         for (int pass = 0; pass < npass; ++pass) {
             const int c0 = pass * CPP + gl * VEC;
             float acc[VEC];
 #pragma unroll
             for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
-            if (c0 < p.ncols) accumulate<T, VEC, U, HINT>(p, s.y + sub, s.z, P, c0, acc, pol);
+            if (c0 < p.ncols) accumulate_simple<T, VEC, U>(p, s.y + sub, s.z, P, c0, acc);
 #pragma unroll
             for (int off = G; off < 32; off <<= 1)
 #pragma unroll
@@ -374,7 +320,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 4 ? 4 : 3) residue_kernel(co
     for (int pass = 0; pass < npass; ++pass) {
         const int c0 = pass * CPP + gl * VEC;
         if (c0 >= p.ncols) break;
-        stream_rows<T, VEC, U, HINT>(p, r_lo, r_hi, c0, pol);
+        stream_lean<T, VEC, U>(p, r_lo, r_hi, c0);
     }
 }
 

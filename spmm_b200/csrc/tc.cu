@@ -22,7 +22,7 @@
 // Warp roles (288 threads): warps 0-3 epilogue (tcgen05.ld of TMEM lanes
 // 32w..32w+31 -> coalesced fp32 C rows), warp 4 TMEM allocation + MMA issue
 // (one thread), warps 5-8 producers (cp.async 16-byte gathers of B rows and
-// value tiles into a 7-stage mbarrier ring; B-row indices staged in smem).  Two TMEM accumulators let the
+// value tiles into a 16-stage mbarrier ring; B-row indices staged in smem).  Two TMEM accumulators let the
 // epilogue of one unit overlap the MMAs of the next.
 //
 // Every mbarrier wait is bounded: on time-out the kernel records a code in the
@@ -46,7 +46,7 @@ namespace {
 constexpr int R = 32;            // window rows = MMA N
 constexpr int KT = 16;           // condensed columns per tile = MMA K (16-bit inputs)
 constexpr int MB = 128;          // output columns per unit = MMA M
-constexpr int STAGES = 7;
+constexpr int STAGES = 16;
 constexpr int IDX_TILES = 32;           // tile column indices staged per producer warp per refill
 constexpr int PANEL_BYTES = MB * KT * 2;  // 4096
 constexpr int VAL_BYTES = R * KT * 2;     // 1024
@@ -331,7 +331,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_kernel(const TcParams p)
     }
 }
 
-constexpr size_t kSmemBytes = 1024 + STAGES * STAGE_BYTES + 4 * IDX_TILES * KT * 4 + 256;  // < 48 KB
+// Tail: 2 * STAGES + 5 mbarriers, the TMEM address and the abort flag.
+constexpr size_t kBarBytes = (2 * STAGES + 5) * 8 + 8;
+constexpr size_t kSmemBytes = 1024 + STAGES * STAGE_BYTES + 4 * IDX_TILES * KT * 4 + (kBarBytes + 127) / 128 * 128;  // ~89 KB
 
 template <typename X>
 tcaspmm_status upload_vec(Shard *sh, X **dst, const std::vector<X> &v, const char *what)
@@ -393,7 +395,11 @@ tcaspmm_status tc_upload(const tcaspmm_csr &, tcaspmm_dtype dt, Shard *sh)
     int nsm = 148;
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, sh->device);
     sh->num_sms = nsm;
-    return TCASPMM_OK;
+    // More than 48 KB of dynamic shared memory needs the opt-in, per device.
+    cudaError_t e = cudaFuncSetAttribute(tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    return e == cudaSuccess ? TCASPMM_OK : cuda_fail(e, "tc kernel shared-memory opt-in");
 }
 
 tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int64_t ldb, float *dC, int64_t ldc,
