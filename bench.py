@@ -122,6 +122,14 @@ class ClockSampler:
                 "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
 
 
+def host_threads() -> int:
+    """All host threads this process may use (torchrun sets OMP_NUM_THREADS=1, so ask the OS)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
 def algorithmic_bytes(M, K, nnz, N, elem):
     return (M + 1) * 4 + nnz * (4 + elem) + K * N * elem + M * N * 4
 
@@ -162,7 +170,7 @@ def run_reference(args, wl):
     B = T.gen_dense(A.ncol, N, 1, "f32")
     if dt != "f32":
         B = B.astype(np.float16).astype(np.float32)
-    threads = oracle.max_threads()
+    threads = host_threads()
     vals = A.values()
     t0 = time.perf_counter()
     oracle.spmm_f32(A.row_ptr, A.col, vals, B, threads)  # one full pass: sizes the sample
@@ -331,7 +339,7 @@ def main():
 
         Bf = Bfull.astype(np.float32) if dt != "bf16" else torch.from_numpy(Bfull.view(np.int16)).view(
             torch.bfloat16).float().numpy()
-        threads = oracle.max_threads()
+        threads = host_threads()
         v, sample = cpu_reference(A, Bf, threads)
         cpu = {"value": round(v, 3), "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
 

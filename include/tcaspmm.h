@@ -193,6 +193,15 @@ tcaspmm_status tcaspmm_plan_sync_check(tcaspmm_plan *plan);
 tcaspmm_status tcaspmm_schedule_coverage(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt,
                                          int32_t *cover, int8_t *kind, tcaspmm_plan_stats *stats);
 
+/* ------------------------------------------------------------ self-test
+ * Failure detection of the tensor-core kernel without a GPU fault: launches one
+ * tensor-core window on `device` whose producer never issues its copies, so the
+ * MMA thread's bounded wait runs out after `wait_cycles` SM clocks; the kernel
+ * records the time-out, stops, frees its tensor memory and returns, and the
+ * context stays usable.  Returns TCASPMM_ERR_TIMEOUT (the designed outcome) with
+ * the device error word in *err_code; TCASPMM_OK would mean no time-out was seen. */
+tcaspmm_status tcaspmm_selftest_tc_timeout(int device, unsigned long long wait_cycles, int *err_code);
+
 /* ------------------------------------------------- reference entry point
  * Same signature, argument meaning and behaviour as our_spmm_balanced
  * (src/our_spmm.cuh:4, src/our_spmm.cu:478-594): host CSR with binary16 values,

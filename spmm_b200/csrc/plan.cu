@@ -80,6 +80,7 @@ tcaspmm_status build_shard(const tcaspmm_csr &A, tcaspmm_dtype dt, int device, i
     sh->device = device;
     sh->col_begin = col_begin;
     sh->ncols = ncols;
+    sh->K = A.ncol;
     DeviceGuard g(device);
     int nsm = 148;
     cudaError_t e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device);

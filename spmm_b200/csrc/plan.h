@@ -12,6 +12,7 @@ namespace tca {
 struct Shard {
     int device = 0;
     int64_t col_begin = 0, ncols = 0;
+    int64_t K = 0;  // rows of B
     Schedule sched;  // host schedule; large arrays are released after upload
     std::vector<void *> allocs;
     int64_t bytes = 0;
@@ -39,6 +40,13 @@ struct Shard {
     int32_t *tc_cols = nullptr;   // KT B-row indices per tile
     void *tc_vals = nullptr;      // R x KT values per tile, shared-memory image
     Int2 *tc_fallback = nullptr;  // one row range per window (unaligned B: CUDA cores)
+    bool tc_tma = true;           // TMA producer (else 16-byte cp.async gathers)
+    // Tensor maps over the last B block launched (rebuilt when B or ldb change);
+    // opaque storage for two 128-byte CUtensorMap objects.
+    alignas(64) mutable unsigned char maps[256] = {};
+    mutable bool maps_valid = false;
+    mutable const void *maps_ptr = nullptr;
+    mutable int64_t maps_ldb = 0;
 
     int *err = nullptr;  // device error word (bounded waits that ran out)
 };

@@ -12,27 +12,39 @@
 // N = R (window rows -> TMEM columns), K = 16 per tile, fp32 accumulation in
 // TMEM across the window's tiles.
 //
-// Shared-memory operands, canonical no-swizzle layouts (16-byte core-matrix rows):
-//   A = B panel, MN-major: 16 gathered B rows x 128 columns, core matrix =
-//       8 k-rows x 8 columns (128 B); columns step SBO = 256 B, k step LBO = 128 B.
-//   B = value tile, K-major: R rows x 16 k, core matrix = 8 rows x 8 k;
-//       k step LBO = 128 B, rows step SBO = 256 B.  The host stores each tile's
-//       values already in this image, so one 16-byte copy per 8 values lands it.
+// Shared-memory operands.  B = value tile, K-major, no swizzle: R rows x 16 k,
+// core matrix = 8 rows x 8 k, k step LBO = 128 B, rows step SBO = 256 B; the
+// host stores each tile's values in exactly this image.  A = B panel (16
+// gathered B rows x 128 columns), MN-major, filled by one of two producers:
+//   TMA producer (default): 128-byte-swizzled atoms of 8 k-rows x 64 columns;
+//       the two 64-column halves are LBO = 2 KB apart, the two groups of 8
+//       k-rows SBO = 1 KB apart.  One lane issues, per tile, either 2 TMA tile
+//       loads of a 64 x 16 box (when the tile's 16 B rows are consecutive, as in
+//       dense windows) or 8 tile::gather4 loads of 4 rows each, plus one 1 KB
+//       cp.async.bulk of the value tile; the 2-D tensor map over B writes the
+//       swizzle and zero-fills columns past N.
+//   cp.async producer: no swizzle, core matrix = 8 k-rows x 8 columns (128 B);
+//       columns step SBO = 256 B, k step LBO = 128 B; 4 warps of 16-byte
+//       cp.async gathers.
 //
-// Warp roles (288 threads): warps 0-3 epilogue (tcgen05.ld of TMEM lanes
-// 32w..32w+31 -> coalesced fp32 C rows), warp 4 TMEM allocation + MMA issue
-// (one thread), warps 5-8 producers (cp.async 16-byte gathers of B rows and
-// value tiles into a 16-stage mbarrier ring; B-row indices staged in smem).  Two TMEM accumulators let the
-// epilogue of one unit overlap the MMAs of the next.
+// Warp roles: warps 0-3 epilogue (tcgen05.ld of TMEM lanes 32w..32w+31 ->
+// coalesced fp32 C rows), warp 4 TMEM allocation + MMA issue (one thread),
+// warp 5 (TMA) or warps 5-8 (cp.async) producers on a 16-stage mbarrier ring,
+// B-row indices staged in shared memory by coalesced warp loads.  Two TMEM
+// accumulators let the epilogue of one unit overlap the MMAs of the next.
 //
 // Every mbarrier wait is bounded: on time-out the kernel records a code in the
-// plan's error word, stops issuing work, drains its MMAs (bounded), frees TMEM
-// and returns; tcaspmm_plan_sync_check reports TCASPMM_ERR_TIMEOUT.
+// plan's error word, stops issuing work, drains its copies and MMAs (bounded),
+// frees TMEM and returns; tcaspmm_plan_sync_check reports TCASPMM_ERR_TIMEOUT and
+// tcaspmm_selftest_tc_timeout exercises that path.
 #include <algorithm>
 #include <climits>
+#include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <vector>
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -52,10 +64,11 @@ constexpr int PANEL_BYTES = MB * KT * 2;  // 4096
 constexpr int VAL_BYTES = R * KT * 2;     // 1024
 constexpr int STAGE_BYTES = PANEL_BYTES + VAL_BYTES;
 constexpr int TMEM_COLS = 2 * R;          // two accumulators
-constexpr int NUM_THREADS = 288;
-constexpr int PRODUCER_THREADS = 128;
+constexpr int PRODUCER_THREADS = 128;  // cp.async producer
 constexpr int EPI_THREADS = 128;
-constexpr unsigned long long WAIT_CYCLES = 4ull << 30;  // ~2 s at 2 GHz
+constexpr unsigned long long WAIT_CYCLES = 4ull << 30;  // ~2 s at 2 GHz: no legitimate wait comes close
+
+template <bool TMA> constexpr int num_threads() { return TMA ? 192 : 288; }
 
 struct TcParams {
     const int4 *windows;     // {first row, first tile, tiles, rows}
@@ -70,6 +83,8 @@ struct TcParams {
     int n_units;
     int nfb;                 // column blocks of 128
     int *err;
+    unsigned long long wait_cycles;  // bound of every mbarrier wait
+    int stall_test;          // self-test: the producer issues no copies, so waits must time out
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -99,14 +114,14 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar)
 
 // Bounded wait: false (and the abort flag raised, error recorded) on time-out.
 __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int *abort_flag, int *err,
-                                             int code)
+                                             int code, unsigned long long limit)
 {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = clock64();
     for (;;) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (clock64() - t0 > WAIT_CYCLES) {
+        if (clock64() - t0 > limit) {
             atomicOr(err, code);
             *abort_flag = 1;
             return false;
@@ -124,13 +139,54 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar)
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo)
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// Box of the tensor map (64 columns x 16 rows) at (x, y) -> dst.
+__device__ __forceinline__ void tma_box(uint32_t dst, const void *tmap, int x, int y, uint32_t bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(tmap), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+// 4 rows (y0..y3) x 64 columns from x of the gather tensor map -> dst.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const void *tmap, int x, int y0, int y1, int y2, int y3,
+                                            uint32_t bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+        "l"(tmap), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_copy(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout)
 {
     // tcgen05 shared-memory descriptor: start address, leading / stride byte
-    // offsets (all >> 4), version 1 (bits 46-47), no swizzle (bits 61-63 = 0).
+    // offsets (all >> 4), version 1 (bits 46-47), layout type (bits 61-63:
+    // 0 no swizzle, 2 128-byte swizzle).
     return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
-           ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46);
+           ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
 }
+
+// The two tensor maps over the B block of a launch: box 64 x 1 (gather4) and
+// box 64 x 16 (consecutive rows), both 128-byte swizzled.
+struct BMaps {
+    CUtensorMap gather;
+    CUtensorMap box;
+};
 
 template <bool BF16>
 __device__ __forceinline__ constexpr uint32_t instr_desc()
@@ -179,8 +235,8 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <bool BF16>
-__global__ void __launch_bounds__(NUM_THREADS, 1) tc_kernel(const TcParams p)
+template <bool BF16, bool TMA>
+__global__ void __launch_bounds__(num_threads<TMA>(), 1) tc_kernel(const TcParams p, const __grid_constant__ BMaps maps)
 {
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte aligned stage ring, then barriers.
@@ -201,7 +257,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_kernel(const TcParams p)
 
     if (tid == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(smem_u32(&full[s]), PRODUCER_THREADS);
+            // TMA: the producer's arrive.expect_tx (TMA completes the bytes);
+            // cp.async: one noinc arrive per producer thread.
+            mbar_init(smem_u32(&full[s]), TMA ? 1 : PRODUCER_THREADS);
             mbar_init(smem_u32(&empty[s]), 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -223,8 +281,68 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_kernel(const TcParams p)
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
 
-    if (warp >= 5) {
-        // ------------------------------ producers ------------------------------
+    if (TMA && warp == 5) {
+        // ---------------------------- TMA producer -----------------------------
+        // The warp stages the B-row indices of up to IDX_TILES tiles in shared
+        // memory with one coalesced load; lane 0 then issues per tile 2 box
+        // loads (consecutive rows) or 8 gather4 loads, and one bulk copy of the
+        // value tile.  Abort decisions are warp-uniform.
+        uint32_t g = 0;
+        bool ok = true;
+        const void *tm_g = &maps.gather;
+        const void *tm_b = &maps.box;
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(tm_g) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(tm_b) : "memory");
+        }
+        for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
+            const int4 w = p.windows[p.order[u / p.nfb]];
+            const int n0 = (u % p.nfb) * MB;
+            for (int t0 = 0; ok && t0 < w.z; t0 += IDX_TILES) {
+                const int nt = min(IDX_TILES, w.z - t0);
+                __syncwarp();  // previous indices consumed
+                for (int q = lane; q < nt * KT; q += 32) idxbuf[q] = __ldg(p.tile_cols + ((long long)w.y + t0) * KT + q);
+                __syncwarp();  // indices visible to the warp
+                for (int t = 0; t < nt; ++t, ++g) {
+                    const int s = g % STAGES;
+                    ok = __all_sync(0xffffffffu, wait_bounded(smem_u32(&empty[s]), ((g / STAGES) & 1) ^ 1, abort_flag,
+                                                              p.err, 1, p.wait_cycles));
+                    if (!ok) break;
+                    if (lane == 0 && !p.stall_test) {
+                        const uint32_t fb = smem_u32(&full[s]);
+                        const uint32_t panel = smem_u32(smem + s * STAGE_BYTES);
+                        const int32_t *ix = idxbuf + t * KT;
+                        mbar_expect_tx(fb, STAGE_BYTES);
+                        if (ix[KT - 1] - ix[0] == KT - 1) {
+                            // Columns are distinct and ascending, so a span of 15
+                            // means 16 consecutive B rows: two 64 x 16 boxes.
+                            tma_box(panel, tm_b, n0, ix[0], fb);
+                            tma_box(panel + 2048, tm_b, n0 + 64, ix[0], fb);
+                        } else {
+#pragma unroll
+                            for (int c = 0; c < 2; ++c)
+#pragma unroll
+                                for (int q = 0; q < 4; ++q)
+                                    tma_gather4(panel + c * 2048 + (q >> 1) * 1024 + (q & 1) * 512, tm_g, n0 + 64 * c,
+                                                ix[4 * q], ix[4 * q + 1], ix[4 * q + 2], ix[4 * q + 3], fb);
+                        }
+                        bulk_copy(panel + PANEL_BYTES, p.tile_vals + ((long long)w.y + t0 + t) * (R * KT), VAL_BYTES,
+                                  fb);
+                    }
+                }
+            }
+        }
+        // Drain: the copies of the last STAGES tiles must have landed before the
+        // CTA may exit (already true unless the kernel is aborting).
+        if (lane == 0 && !p.stall_test) {
+            int no_abort = 0;
+            for (uint32_t k = g > (uint32_t)STAGES ? g - STAGES : 0; k < g; ++k)
+                wait_bounded(smem_u32(&full[k % STAGES]), (k / STAGES) & 1, (volatile int *)&no_abort, p.err, 16,
+                             p.wait_cycles);
+        }
+        __syncwarp();
+    } else if (!TMA && warp >= 5) {
+        // --------------------------- cp.async producers -------------------------
         // Each producer warp stages the B-row indices of up to IDX_TILES tiles in
         // its own shared-memory slice with one cooperative load, so no cp.async
         // waits on a dependent load.  Only warp-level syncs are used, and every
@@ -248,9 +366,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_kernel(const TcParams p)
                 __syncwarp();  // indices visible to the warp
                 for (int t = 0; t < nt; ++t, ++g) {
                     const int s = g % STAGES;
-                    ok = __all_sync(0xffffffffu,
-                                    wait_bounded(smem_u32(&empty[s]), ((g / STAGES) & 1) ^ 1, abort_flag, p.err, 1));
+                    ok = __all_sync(0xffffffffu, wait_bounded(smem_u32(&empty[s]), ((g / STAGES) & 1) ^ 1, abort_flag,
+                                                              p.err, 1, p.wait_cycles));
                     if (!ok) break;
+                    if (p.stall_test) continue;
                     const long long tile = (long long)w.y + t0 + t;
                     const uint32_t panel = smem_u32(smem + s * STAGE_BYTES);
 #pragma unroll
@@ -275,20 +394,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_kernel(const TcParams p)
             for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x, ++i) {
                 const int4 w = p.windows[p.order[u / p.nfb]];
                 const uint32_t a = i & 1;
-                if (!wait_bounded(smem_u32(&acce[a]), ((i >> 1) & 1) ^ 1, abort_flag, p.err, 2)) break;
+                if (!wait_bounded(smem_u32(&acce[a]), ((i >> 1) & 1) ^ 1, abort_flag, p.err, 2, p.wait_cycles)) break;
                 tc_fence_after();
                 const uint32_t dcol = tmem + a * R;
                 for (int t = 0; t < w.z; ++t, ++g) {
                     const int s = g % STAGES;
-                    if (!wait_bounded(smem_u32(&full[s]), (g / STAGES) & 1, abort_flag, p.err, 2)) {
+                    if (!wait_bounded(smem_u32(&full[s]), (g / STAGES) & 1, abort_flag, p.err, 2, p.wait_cycles)) {
                         ok = false;
                         break;
                     }
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    if (!TMA) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // cp.async wrote it
                     tc_fence_after();
                     const uint32_t panel = smem_u32(smem + s * STAGE_BYTES);
-                    const uint64_t adesc = smem_desc(panel, 128, 256);
-                    const uint64_t bdesc = smem_desc(panel + PANEL_BYTES, 128, 256);
+                    const uint64_t adesc = TMA ? smem_desc(panel, 2048, 1024, 2)   // MN-major, 128-byte swizzle
+                                               : smem_desc(panel, 128, 256, 0);    // MN-major, no swizzle
+                    const uint64_t bdesc = smem_desc(panel + PANEL_BYTES, 128, 256, 0);  // K-major, no swizzle
                     mma_f16(dcol, adesc, bdesc, idesc, t > 0 ? 1u : 0u);
                     mma_commit(smem_u32(&empty[s]));
                 }
@@ -298,16 +418,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_kernel(const TcParams p)
             // Drain: every MMA issued above has completed once `drain` flips.
             mma_commit(smem_u32(drain));
             int dummy = 0;
-            wait_bounded(smem_u32(drain), 0, (volatile int *)&dummy, p.err, 8);
+            wait_bounded(smem_u32(drain), 0, (volatile int *)&dummy, p.err, 8, p.wait_cycles);
         }
         __syncwarp();
-    } else {
+    } else if (warp < 4) {
         // ------------------------------ epilogue -------------------------------
         uint32_t i = 0;
         for (int u = blockIdx.x; u < p.n_units; u += gridDim.x, ++i) {
             const int4 w = p.windows[p.order[u / p.nfb]];
             const uint32_t a = i & 1;
-            if (!__all_sync(0xffffffffu, wait_bounded(smem_u32(&accf[a]), (i >> 1) & 1, abort_flag, p.err, 4))) break;
+            if (!__all_sync(0xffffffffu,
+                            wait_bounded(smem_u32(&accf[a]), (i >> 1) & 1, abort_flag, p.err, 4, p.wait_cycles)))
+                break;
             tc_fence_after();
             float v[32];
             tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + a * R, v);
@@ -349,6 +471,62 @@ tcaspmm_status upload_vec(Shard *sh, X **dst, const std::vector<X> &v, const cha
     sh->bytes += (int64_t)(sizeof(X) * v.size());
     e = cudaMemcpy(*dst, v.data(), sizeof(X) * v.size(), cudaMemcpyHostToDevice);
     return e == cudaSuccess ? TCASPMM_OK : cuda_fail(e, what);
+}
+
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime
+// (no link-time dependency on libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn()
+{
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)f;
+    });
+    return fn;
+}
+
+// Tensor maps over a B block of ncols columns x K rows (x = column, zero fill
+// beyond ncols; y = B row), 128-byte swizzle, boxes 64 x 1 and 64 x 16.
+tcaspmm_status encode_b_maps(tcaspmm_dtype dt, const void *dB, int64_t ncols, int64_t K, int64_t ldb, BMaps *m)
+{
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(TCASPMM_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[2] = {(cuuint64_t)ncols, (cuuint64_t)K};
+    const cuuint64_t strides[1] = {(cuuint64_t)ldb * 2};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapDataType ty = dt == TCASPMM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const cuuint32_t box1[2] = {64, 1}, box16[2] = {64, 16};
+    CUresult r = fn(&m->gather, ty, 2, const_cast<void *>(dB), dims, strides, box1, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r == CUDA_SUCCESS)
+        r = fn(&m->box, ty, 2, const_cast<void *>(dB), dims, strides, box16, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? TCASPMM_OK : fail(TCASPMM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+}
+
+static_assert(sizeof(BMaps) <= sizeof(Shard::maps), "tensor-map storage in Shard");
+
+template <bool BF16, bool TMA>
+cudaError_t smem_optin()
+{
+    return cudaFuncSetAttribute(tc_kernel<BF16, TMA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+}
+
+template <bool TMA>
+void launch_kernel(bool bf16, int grid, const TcParams &p, const BMaps &maps, cudaStream_t st)
+{
+    if (bf16)
+        tc_kernel<true, TMA><<<grid, num_threads<TMA>(), kSmemBytes, st>>>(p, maps);
+    else
+        tc_kernel<false, TMA><<<grid, num_threads<TMA>(), kSmemBytes, st>>>(p, maps);
 }
 
 }  // namespace
@@ -395,10 +573,14 @@ tcaspmm_status tc_upload(const tcaspmm_csr &, tcaspmm_dtype dt, Shard *sh)
     int nsm = 148;
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, sh->device);
     sh->num_sms = nsm;
+    // Producer: TMA unless TCASPMM_TC_PRODUCER=cpasync.
+    const char *prod = std::getenv("TCASPMM_TC_PRODUCER");
+    sh->tc_tma = !(prod && std::strcmp(prod, "cpasync") == 0);
     // More than 48 KB of dynamic shared memory needs the opt-in, per device.
-    cudaError_t e = cudaFuncSetAttribute(tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    cudaError_t e = smem_optin<false, true>();
+    if (e == cudaSuccess) e = smem_optin<true, true>();
+    if (e == cudaSuccess) e = smem_optin<false, false>();
+    if (e == cudaSuccess) e = smem_optin<true, false>();
     return e == cudaSuccess ? TCASPMM_OK : cuda_fail(e, "tc kernel shared-memory opt-in");
 }
 
@@ -422,13 +604,102 @@ tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int6
     p.nfb = (int)((sh.ncols + MB - 1) / MB);
     p.n_units = sh.n_windows * p.nfb;
     p.err = sh.err;
+    p.wait_cycles = WAIT_CYCLES;
+    p.stall_test = 0;
     const int grid = std::min(p.n_units, 4 * sh.num_sms);
-    if (dt == TCASPMM_BF16)
-        tc_kernel<true><<<grid, NUM_THREADS, kSmemBytes, st>>>(p);
-    else
-        tc_kernel<false><<<grid, NUM_THREADS, kSmemBytes, st>>>(p);
+    if (sh.tc_tma) {
+        // Tensor maps depend on the B block: rebuilt only when it changes.
+        if (!(sh.maps_valid && sh.maps_ptr == dB && sh.maps_ldb == ldb)) {
+            sh.maps_valid = false;
+            tcaspmm_status ms = encode_b_maps(dt, dB, sh.ncols, sh.K, ldb, (BMaps *)sh.maps);
+            if (ms != TCASPMM_OK) return ms;
+            sh.maps_valid = true;
+            sh.maps_ptr = dB;
+            sh.maps_ldb = ldb;
+        }
+        launch_kernel<true>(dt == TCASPMM_BF16, grid, p, *(const BMaps *)sh.maps, st);
+    } else {
+        launch_kernel<false>(dt == TCASPMM_BF16, grid, p, BMaps{}, st);
+    }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TCASPMM_OK : cuda_fail(e, "tc kernel launch");
 }
 
 }  // namespace tca
+
+using namespace tca;
+
+// Failure-detection self-test: one tensor-core window whose producer issues no
+// copies (a flag nothing sets), so the MMA thread's bounded wait must run out
+// after `wait_cycles`; the kernel records the time-out, frees its TMEM and
+// returns, and the context stays usable.  Returns TCASPMM_ERR_TIMEOUT with the
+// device error word in *err_code when that happened as designed.
+extern "C" tcaspmm_status tcaspmm_selftest_tc_timeout(int device, unsigned long long wait_cycles, int *err_code)
+{
+    clear_error();
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    if (!tc_supported()) return fail(TCASPMM_ERR_UNSUPPORTED, "device %d is not sm_100", device);
+    const int4 win = make_int4(0, 0, 1, R);
+    const int32_t order = 0;
+    const std::vector<int32_t> cols(KT, 0);
+    const std::vector<uint16_t> vals(R * KT, 0);
+    void *d_win = nullptr, *d_order = nullptr, *d_cols = nullptr, *d_vals = nullptr, *d_b = nullptr, *d_c = nullptr;
+    int *d_err = nullptr;
+    tcaspmm_status st = TCASPMM_OK;
+    auto alloc = [&](void **ptr, size_t n) {
+        if (st == TCASPMM_OK && (e = cudaMalloc(ptr, n)) != cudaSuccess) st = cuda_fail(e, "self-test allocation");
+    };
+    alloc(&d_win, sizeof(win));
+    alloc(&d_order, sizeof(order));
+    alloc(&d_cols, cols.size() * 4);
+    alloc(&d_vals, vals.size() * 2);
+    alloc(&d_b, KT * MB * 2);
+    alloc(&d_c, R * MB * 4);
+    alloc((void **)&d_err, sizeof(int));
+    BMaps maps;
+    if (st == TCASPMM_OK) {
+        cudaMemcpy(d_win, &win, sizeof(win), cudaMemcpyHostToDevice);
+        cudaMemcpy(d_order, &order, sizeof(order), cudaMemcpyHostToDevice);
+        cudaMemcpy(d_cols, cols.data(), cols.size() * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(d_vals, vals.data(), vals.size() * 2, cudaMemcpyHostToDevice);
+        cudaMemset(d_b, 0, KT * MB * 2);
+        cudaMemset(d_err, 0, sizeof(int));
+        st = encode_b_maps(TCASPMM_F16, d_b, MB, KT, MB, &maps);
+    }
+    if (st == TCASPMM_OK) {
+        TcParams p;
+        p.windows = (const int4 *)d_win;
+        p.order = (const int32_t *)d_order;
+        p.tile_cols = (const int32_t *)d_cols;
+        p.tile_vals = (const uint16_t *)d_vals;
+        p.B = d_b;
+        p.ldb = MB;
+        p.C = (float *)d_c;
+        p.ldc = MB;
+        p.ncols = MB;
+        p.nfb = 1;
+        p.n_units = 1;
+        p.err = d_err;
+        p.wait_cycles = wait_cycles;
+        p.stall_test = 1;
+        e = smem_optin<false, true>();
+        if (e == cudaSuccess) {
+            launch_kernel<true>(false, 1, p, maps, 0);
+            e = cudaGetLastError();
+        }
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        int err = 0;
+        if (e == cudaSuccess) e = cudaMemcpy(&err, d_err, sizeof(int), cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) {
+            st = cuda_fail(e, "self-test kernel");
+        } else {
+            if (err_code) *err_code = err;
+            st = err ? fail(TCASPMM_ERR_TIMEOUT, "tensor-core wait timed out as designed (code 0x%x)", err)
+                     : fail(TCASPMM_OK, "no time-out recorded");
+        }
+    }
+    for (void *ptr : {d_win, d_order, d_cols, d_vals, d_b, d_c, (void *)d_err})
+        if (ptr) cudaFree(ptr);
+    return st;
+}

@@ -223,3 +223,17 @@ def test_tensor_core_integer_values_bit_exact():
     out, st = run(A, B, "f16")
     assert st["tc_windows"] > 0
     np.testing.assert_array_equal(out, reference(A, B, "f16").astype(np.float32))
+
+
+def test_tensor_core_wait_time_out_is_reported_and_recoverable():
+    """A wait that nothing will satisfy ends in TCASPMM_ERR_TIMEOUT, not a hang, and the GPU stays usable."""
+    import ctypes
+
+    fn = T.lib.tcaspmm_selftest_tc_timeout
+    fn.argtypes = [ctypes.c_int, ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_int)]
+    fn.restype = ctypes.c_int
+    code = ctypes.c_int(0)
+    status = fn(0, 200_000_000, ctypes.byref(code))  # ~0.1 s of SM clocks
+    assert status == T.Status.TIMEOUT, T.last_error()
+    assert code.value & 2  # the MMA thread's wait on the producer ran out
+    check(T.gen_uniform(256, 256, 0.4, 14), 128, "f16")  # the context still works
