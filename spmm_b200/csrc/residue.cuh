@@ -141,34 +141,33 @@ __device__ __forceinline__ void add_l2(const float *c, float (&a)[VEC])
     }
 }
 
-// acc += sum_{j = b, b+stride, ... < e} val[j] * B[col[j]][c0 .. c0+VEC): U
-// indices, then U independent B loads, then the FMAs (no prefetch; few registers).
+// acc += sum_{j in [b, e)} val[j] * B[col[j]][c0 .. c0+VEC): full chunks of U
+// without predicates (U indices, U independent B loads, U FMAs), then the
+// remainder one nonzero at a time.
 template <typename T, int VEC, int U>
-__device__ __forceinline__ void accumulate_simple(const ResidueParams &p, int b, int e, int stride, int c0,
-                                                  float (&acc)[VEC])
+__device__ __forceinline__ void accumulate_lean(const ResidueParams &p, int b, const int e, int c0, float (&acc)[VEC])
 {
     const T *__restrict__ B = static_cast<const T *>(p.B) + c0;
     const T *__restrict__ val = static_cast<const T *>(p.val);
-    for (int j = b; j < e; j += U * stride) {
+    for (; b + U <= e; b += U) {
         int cc[U];
         float vv[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            const int jj = j + u * stride;
-            const bool ok = jj < e;
-            cc[u] = ok ? __ldg(p.col + jj) : -1;
-            vv[u] = ok ? to_f<T>(__ldg(val + jj)) : 0.0f;
+            cc[u] = __ldg(p.col + b + u);
+            vv[u] = to_f<T>(__ldg(val + b + u));
         }
         Raw<T, VEC> rb[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            if (cc[u] >= 0)
-                load_raw<T, VEC>(B + (long long)cc[u] * p.ldb, rb[u]);
-            else
-                zero_raw<T, VEC>(rb[u]);
-        }
+        for (int u = 0; u < U; ++u) load_raw<T, VEC>(B + (long long)cc[u] * p.ldb, rb[u]);
 #pragma unroll
         for (int u = 0; u < U; ++u) fma_raw<T, VEC>(vv[u], rb[u], acc);
+    }
+    for (; b < e; ++b) {
+        Raw<T, VEC> rb;
+        const float v = to_f<T>(__ldg(val + b));
+        load_raw<T, VEC>(B + (long long)__ldg(p.col + b) * p.ldb, rb);
+        fma_raw<T, VEC>(v, rb, acc);
     }
 }
 
@@ -258,14 +257,17 @@ __global__ void __launch_bounds__(256, 4) residue_kernel(const ResidueParams p)
 
     if (warp < p.n_segs) {
         const int4 s = p.segs[warp];
-        // Group `sub` takes nonzeros s.y + sub, s.y + sub + P, ...; the groups
-        // are then reduced with shuffles in a fixed order.
+        // Group `sub` takes a contiguous 1/P of the segment; the groups are then
+        // reduced with shuffles in a fixed order.
+        const int len = s.z - s.y;
+        const int jb = s.y + (int)((long long)len * sub / P);
+        const int je = s.y + (int)((long long)len * (sub + 1) / P);
         for (int pass = 0; pass < npass; ++pass) {
             const int c0 = pass * CPP + gl * VEC;
             float acc[VEC];
 #pragma unroll
             for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
-            if (c0 < p.ncols) accumulate_simple<T, VEC, U>(p, s.y + sub, s.z, P, c0, acc);
+            if (c0 < p.ncols) accumulate_lean<T, VEC, U>(p, jb, je, c0, acc);
 #pragma unroll
             for (int off = G; off < 32; off <<= 1)
 #pragma unroll

@@ -1,0 +1,125 @@
+"""torch custom op for GCN / GraphSAGE aggregation: ``torch.ops.tcaspmm.spmm``.
+
+    Y = torch.ops.tcaspmm.spmm(crow, col, val, X)      # Y = A @ X, fp32, shape (M, N)
+
+``crow`` (int32/int64, M+1), ``col`` (int32/int64, nnz) and ``val`` (nnz) describe A in
+CSR on the host or on X's device; ``X`` is a CUDA tensor (K x N, float32 / float16 /
+bfloat16).  The op runs tcaspmm's plan-based C-ABI path (``spmm_b200/lib/libtcaspmm.so``)
+on X's current stream: a plan (host preprocessing + one upload of A) is built the
+first time a given (A, N, dtype, device) is seen and reused afterwards, so a GNN layer
+pays the preprocessing once per graph.  The gradient with respect to X is
+``A^T @ dY``, computed with a second cached plan over the transpose of A; A's values
+are treated as constants (the graph does not train).  There is no CPU or PyTorch
+fallback: without the library or a CUDA device the op raises.
+"""
+from __future__ import annotations
+
+from typing import Dict, Tuple
+
+import numpy as np
+import torch
+
+from . import CSR, Plan, as_dtype
+
+_PLANS: Dict[Tuple, Plan] = {}
+_MAX_PLANS = 16
+
+
+def _key(crow: torch.Tensor, col: torch.Tensor, val: torch.Tensor, N: int, dt, dev: int, transposed: bool) -> Tuple:
+    return (crow.data_ptr(), col.data_ptr(), val.data_ptr(), tuple(crow.shape), tuple(col.shape), crow.device.type,
+            int(N), str(dt), dev, transposed, getattr(val, "_version", 0))
+
+
+def _host_csr(crow: torch.Tensor, col: torch.Tensor, val: torch.Tensor, ncol: int, transposed: bool) -> CSR:
+    rp = crow.detach().to("cpu", torch.int64).numpy()
+    ci = col.detach().to("cpu", torch.int64).numpy()
+    va = val.detach().to("cpu", torch.float32).numpy()
+    M = rp.shape[0] - 1
+    if not transposed:
+        return CSR(M, ncol, rp, ci.astype(np.int32), va)
+    # CSR of A^T: stable sort of the nonzeros by column keeps rows ascending.
+    rows = np.repeat(np.arange(M, dtype=np.int64), np.diff(rp))
+    order = np.argsort(ci, kind="stable")
+    trp = np.zeros(ncol + 1, np.int64)
+    np.add.at(trp, ci + 1, 1)
+    return CSR(ncol, M, np.cumsum(trp), rows[order].astype(np.int32), va[order])
+
+
+def _plan(crow, col, val, ncol: int, X: torch.Tensor, transposed: bool) -> Plan:
+    dt = as_dtype(X.dtype)
+    dev = X.device.index if X.device.index is not None else torch.cuda.current_device()
+    k = _key(crow, col, val, X.shape[1], dt, dev, transposed)
+    p = _PLANS.get(k)
+    if p is None:
+        if len(_PLANS) >= _MAX_PLANS:
+            _PLANS.pop(next(iter(_PLANS))).close()
+        p = Plan(_host_csr(crow, col, val, ncol, transposed), X.shape[1], dt, 1, [dev])
+        _PLANS[k] = p
+    return p
+
+
+def clear_plan_cache() -> None:
+    while _PLANS:
+        _PLANS.popitem()[1].close()
+
+
+@torch.library.custom_op("tcaspmm::spmm", mutates_args=())
+def spmm(crow: torch.Tensor, col: torch.Tensor, val: torch.Tensor, X: torch.Tensor) -> torch.Tensor:
+    if not X.is_cuda:
+        raise ValueError("tcaspmm::spmm needs X on a CUDA device")
+    X = X.contiguous()
+    M = crow.shape[0] - 1
+    p = _plan(crow, col, val, X.shape[0], X, transposed=False)
+    out = torch.empty((M, X.shape[1]), device=X.device, dtype=torch.float32)
+    p.execute1(X, out, torch.cuda.current_stream(X.device))
+    return out
+
+
+@spmm.register_fake
+def _(crow, col, val, X):
+    return X.new_empty((crow.shape[0] - 1, X.shape[1]), dtype=torch.float32)
+
+
+@torch.library.custom_op("tcaspmm::spmm_t", mutates_args=())
+def spmm_t(crow: torch.Tensor, col: torch.Tensor, val: torch.Tensor, dY: torch.Tensor, ncol: int) -> torch.Tensor:
+    """A^T @ dY for the backward pass (A given in CSR with ncol columns)."""
+    dY = dY.contiguous()
+    p = _plan(crow, col, val, ncol, dY, transposed=True)
+    out = torch.empty((ncol, dY.shape[1]), device=dY.device, dtype=torch.float32)
+    p.execute1(dY, out, torch.cuda.current_stream(dY.device))
+    return out
+
+
+@spmm_t.register_fake
+def _(crow, col, val, dY, ncol):
+    return dY.new_empty((ncol, dY.shape[1]), dtype=torch.float32)
+
+
+def _setup(ctx, inputs, output):
+    crow, col, val, X = inputs
+    ctx.save_for_backward(crow, col, val)
+    ctx.ncol = X.shape[0]
+    ctx.x_dtype = X.dtype
+
+
+def _backward(ctx, grad):
+    crow, col, val = ctx.saved_tensors
+    g = grad.to(ctx.x_dtype) if ctx.x_dtype != torch.float32 else grad
+    dX = torch.ops.tcaspmm.spmm_t(crow, col, val, g, ctx.ncol)
+    return None, None, None, dX.to(ctx.x_dtype)
+
+
+spmm.register_autograd(_backward, setup_context=_setup)
+
+
+class GCNAggregate(torch.nn.Module):
+    """Y = A_hat @ X with a fixed normalised adjacency A_hat in CSR (the GCN propagation step)."""
+
+    def __init__(self, crow: torch.Tensor, col: torch.Tensor, val: torch.Tensor):
+        super().__init__()
+        self.register_buffer("crow", crow)
+        self.register_buffer("col", col)
+        self.register_buffer("val", val)
+
+    def forward(self, X: torch.Tensor) -> torch.Tensor:
+        return torch.ops.tcaspmm.spmm(self.crow, self.col, self.val, X)
