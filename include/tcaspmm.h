@@ -119,6 +119,17 @@ tcaspmm_status tcaspmm_smtx_read(const char *path, tcaspmm_csr *out);
 /* Write A as .smtx (and "<path>.val" when A->val != NULL). */
 tcaspmm_status tcaspmm_smtx_write(const char *path, const tcaspmm_csr *A);
 
+/* Read a Matrix Market coordinate file (real / integer / pattern; general,
+ * symmetric or skew-symmetric) into CSR: columns sorted per row, repeated
+ * entries summed, symmetric files expanded.  Indices are 1-based as the format
+ * says unless zero_based != 0 (the reference reader's default).  Replaces
+ * mtx_input_to_CSR (src/file_input.cu:64-134). */
+tcaspmm_status tcaspmm_mtx_read(const char *path, int zero_based, tcaspmm_csr *out);
+/* Binary CSR companion ("TCACSR01" header, int64 offsets, int32 columns,
+ * optional float32 values) for graphs too large for text. */
+tcaspmm_status tcaspmm_csrbin_write(const char *path, const tcaspmm_csr *A);
+tcaspmm_status tcaspmm_csrbin_read(const char *path, tcaspmm_csr *out);
+
 /* Dense row-major M x K binary16 matrix -> CSR, dropping zeros.
  * Replaces convert_dense_to_csr (src/miscalleneous.cu:29-65). */
 tcaspmm_status tcaspmm_dense_to_csr(const uint16_t *dense, int64_t M, int64_t K, tcaspmm_csr *out);

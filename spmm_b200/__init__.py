@@ -123,6 +123,9 @@ _sig("tcaspmm_csr_validate", [_P(_CSR)])
 _sig("tcaspmm_smtx_read", [C.c_char_p, _P(_CSR)])
 _sig("tcaspmm_smtx_write", [C.c_char_p, _P(_CSR)])
 _sig("tcaspmm_dense_to_csr", [_vp, _i64, _i64, _P(_CSR)])
+_sig("tcaspmm_mtx_read", [C.c_char_p, C.c_int, _P(_CSR)])
+_sig("tcaspmm_csrbin_write", [C.c_char_p, _P(_CSR)])
+_sig("tcaspmm_csrbin_read", [C.c_char_p, _P(_CSR)])
 _sig("tcaspmm_gen_dense", [_i64, _i64, C.c_uint64, C.c_int, _vp])
 _sig("tcaspmm_gen_uniform", [_i64, _i64, C.c_double, C.c_uint64, _P(_CSR)])
 _sig("tcaspmm_gen_magnitude", [_i64, _i64, C.c_double, C.c_uint64, _P(_CSR)])
@@ -220,6 +223,22 @@ smtx_input_to_CSR = smtx_read
 
 def smtx_write(path: str, A: CSR) -> None:
     _check(lib.tcaspmm_smtx_write(os.fsencode(path), C.byref(A._c())))
+
+
+def mtx_read(path: str, zero_based: bool = False) -> CSR:
+    """Matrix Market coordinate file -> CSR (mtx_input_to_CSR, src/file_input.cu:64-134)."""
+    return _gen(lib.tcaspmm_mtx_read, os.fsencode(path), int(bool(zero_based)))
+
+
+mtx_input_to_CSR = mtx_read
+
+
+def csrbin_write(path: str, A: CSR) -> None:
+    _check(lib.tcaspmm_csrbin_write(os.fsencode(path), C.byref(A._c())))
+
+
+def csrbin_read(path: str) -> CSR:
+    return _gen(lib.tcaspmm_csrbin_read, os.fsencode(path))
 
 
 def convert_dense_to_csr(dense_f16: np.ndarray) -> CSR:

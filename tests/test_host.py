@@ -218,3 +218,38 @@ def test_reference_entry_rejects_mismatched_shapes():
         T.our_spmm_balanced(rp, np.array([0], np.int32), np.array([1.0], np.float16), np.ones((1, 8), np.float16),
                             np.zeros(16, np.float32), 2, 8, 1, 1)
     assert e.value.status == T.Status.INVALID_ARG
+
+
+def test_matrix_market_reader(tmp_path):
+    p = tmp_path / "a.mtx"
+    p.write_text("%%MatrixMarket matrix coordinate real general\n% comment\n3 4 5\n1 2 1.5\n3 1 -2\n1 1 4\n3 4 7\n1 2 0.5\n")
+    A = T.mtx_read(str(p))
+    np.testing.assert_array_equal(A.row_ptr, [0, 2, 2, 4])
+    np.testing.assert_array_equal(A.col, [0, 1, 0, 3])
+    np.testing.assert_allclose(A.val, [4.0, 2.0, -2.0, 7.0])  # repeated (1,2) entries summed
+    p.write_text("%%MatrixMarket matrix coordinate pattern symmetric\n3 3 3\n1 1\n2 1\n3 2\n")
+    S = T.mtx_read(str(p))
+    assert S.val is None
+    np.testing.assert_array_equal(S.to_scipy().toarray(), [[1, 1, 0], [1, 0, 1], [0, 1, 0]])
+    p.write_text("2 2 1\n0 1 3.0\n")  # no banner, 0-based as the reference reader's default
+    Z = T.mtx_read(str(p), zero_based=True)
+    np.testing.assert_array_equal(Z.to_scipy().toarray(), [[0, 3], [0, 0]])
+    p.write_text("2 2 2\n1 1 1\n")
+    with pytest.raises(T.TcaspmmError):
+        T.mtx_read(str(p))
+
+
+def test_binary_csr_roundtrip(tmp_path):
+    for A in (T.gen_rmat(10, 3000, kind="gcn"), T.CSR(4, 3, np.array([0, 1, 1, 1, 2]), np.array([2, 0]), None)):
+        p = str(tmp_path / "a.csrb")
+        T.csrbin_write(p, A)
+        B = T.csrbin_read(p)
+        np.testing.assert_array_equal(A.row_ptr, B.row_ptr)
+        np.testing.assert_array_equal(A.col, B.col)
+        assert (A.val is None) == (B.val is None)
+        if A.val is not None:
+            np.testing.assert_array_equal(A.val, B.val)
+    with open(p, "ab") as f:
+        f.write(b"x")
+    with pytest.raises(T.TcaspmmError):
+        T.csrbin_read(p)
