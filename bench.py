@@ -211,6 +211,11 @@ def main():
     ap.add_argument("--workload", default="gcn", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--epilogue", action="store_true",
+                    help="fused epilogue: C = relu(row_scale * (A B) + bias) stored as bf16")
+    ap.add_argument("--split", default="columns", choices=["columns", "rows"],
+                    help="multi-GPU partition: column blocks of B/C (A replicated) or row blocks of A/C "
+                         "(B replicated)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     wl = WORKLOADS[args.workload]
@@ -240,21 +245,33 @@ def main():
     A = build(T)
     M, K, nnz = A.nrow, A.ncol, A.nnz
     Bfull = T.gen_dense(K, N, 1, dt)  # host, dt (bf16 as uint16 bits)
-    col0, ncols = T.partition_columns(N, dt, world, rank)
-    plan = T.Plan(A, N, dt, rank=rank, world=world, device=local)
+    if args.split == "columns":
+        col0, ncols = T.partition_columns(N, dt, world, rank)
+        row0, mrows = 0, M
+    else:
+        col0, ncols = 0, N
+    plan = T.Plan(A, N, dt, rank=rank, world=world, device=local, split=args.split)
+    if args.split == "rows":
+        row0, mrows = plan.shard_rows(0)
     pst = plan.stats
     Bblk = np.ascontiguousarray(Bfull[:, col0:col0 + ncols])
     Bh = torch.from_numpy(Bblk.view(np.int16) if dt == "bf16" else Bblk)
     if dt == "bf16":
         Bh = Bh.view(torch.bfloat16)
     Bd = Bh.to(dev)
-    Cd = torch.empty((M, max(ncols, 1)), dtype=torch.float32, device=dev)[:, :ncols]
+    cdt = torch.bfloat16 if args.epilogue else torch.float32
+    Cd = torch.empty((mrows, max(ncols, 1)), dtype=cdt, device=dev)[:, :ncols]
+    ep = None
+    if args.epilogue:
+        g = torch.Generator().manual_seed(11)
+        ep = T.Epilogue((torch.rand(mrows, generator=g) + 0.5).to(dev), torch.randn(ncols, generator=g).to(dev),
+                        True, "bf16")
     stream = torch.cuda.current_stream(dev)
     in_l2 = algorithmic_bytes(M, K, nnz, ncols, elem) <= L2_BYTES
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev) if in_l2 else None
 
     def step():
-        plan.execute1(Bd, Cd, stream)
+        plan.execute1(Bd, Cd, stream, epilogue=ep)
 
     def barrier():
         if world > 1:
@@ -301,7 +318,7 @@ def main():
 
     # ---- end to end through the public API: pinned host B -> device, execute, C -> pinned host ----
     Bpin = Bh.pin_memory()
-    Cpin = torch.empty((M, ncols), dtype=torch.float32).pin_memory()
+    Cpin = torch.empty((mrows, ncols), dtype=cdt).pin_memory()
     e2e_steps = max(3, min(args.steps, 50))
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -313,19 +330,19 @@ def main():
     e1.record(stream)
     torch.cuda.synchronize(dev)
     ms_e2e = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
-    h2d = K * N * elem
-    d2h = M * N * 4
+    h2d = K * N * elem * (world if args.split == "rows" else 1)  # row split: every rank copies all of B
+    d2h = M * N * (2 if args.epilogue else 4)
 
     # ---- cuSPARSE baseline on this rank's block (reported, not a target) ----
-    Cs = torch.empty_like(Cd)
+    Cs = torch.empty_like(Cd, dtype=torch.float32)
     try:
         ms_cusparse = max_over_ranks(T.cusparse_spmm(plan, Bd, Cs, warmup=3, iters=max(5, min(args.steps, 50)),
                                                      stream=stream))
-        cs_err = float((Cs - Cd).norm() / max(Cd.norm(), 1e-30))
+        cs_err = float((Cs - Cd).norm() / max(Cd.norm(), 1e-30)) if ep is None else None
     except Exception as e:  # reported
         ms_cusparse, cs_err = None, str(e)
     gemm = None
-    if M * K * elem <= 2**31:
+    if M * K * elem <= 2**31 and args.split == "columns" and ep is None:
         Ad = torch.zeros((M, K), dtype=tdt, device=dev)
         rows = torch.from_numpy(np.repeat(np.arange(M), np.diff(A.row_ptr))).to(dev)
         Ad[rows, torch.from_numpy(A.col.astype(np.int64)).to(dev)] = torch.from_numpy(A.values()).to(dev).to(tdt)
@@ -345,6 +362,8 @@ def main():
 
     peak, peak_kind = load_peaks()
     alg = algorithmic_bytes(M, K, nnz, N, elem)
+    if args.epilogue:  # 16-bit C, plus the row scales and the bias
+        alg += -M * N * 2 + M * 4 + N * 4
     achieved = alg / (ms_step * 1e-3) / 1e9
     kernels_per_step = (1 if pst["residue_row_warps"] + pst["residue_segments"] > 0 else 0) + (
         1 if pst["tc_windows"] > 0 else 0)
@@ -354,11 +373,15 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": dt, "data": "synthetic",
             "config": {"workload": desc, "M": M, "K": K, "N": N, "nnz": nnz,
-                       "parallelism": f"column shards x{world} (A replicated, no data-path collective)",
+                       "parallelism": f"column shards x{world} (A replicated, no data-path collective)"
+                       if args.split == "columns" else
+                       f"row shards x{world} (A split by rows, B replicated, no data-path collective)",
                        "l2": "flushed between steps (2x L2 buffer)" if flush is not None
                        else "inputs larger than L2 (126 MB)",
                        "preprocess_ms": round(pst["preprocess_ms"], 3), "upload_ms": round(pst["upload_ms"], 3),
-                       "tc_windows": pst["tc_windows"], "residue_segments": pst["residue_segments"]},
+                       "tc_windows": pst["tc_windows"], "residue_segments": pst["residue_segments"],
+                       **({"epilogue": "C = relu(row_scale * (A B) + bias) stored as bf16"} if args.epilogue
+                          else {})},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": load_traffic(args.workload),
                          "peak_kind": peak_kind, "algorithmic_bytes": alg,

@@ -163,6 +163,11 @@ tcaspmm_status tcaspmm_gen_skew(int64_t n, int64_t hubs, int64_t hub_nnz, double
  * ceil(N / world) columns rounded up to a 16-byte multiple of dt. */
 tcaspmm_status tcaspmm_partition_columns(int64_t N, tcaspmm_dtype dt, int world, int rank,
                                          int64_t *col_begin, int64_t *col_count);
+/* Row partition of A and C over `parts` GPUs (the 2-D / A-splitting variant for
+ * when A's bytes dominate): row_begin[0..parts] (parts + 1 entries, row_begin[0]
+ * = 0, row_begin[parts] = M), contiguous blocks of about equal cost (nnz + 2 per
+ * row); B is replicated.  Deterministic. */
+tcaspmm_status tcaspmm_partition_rows(const tcaspmm_csr *A, int parts, int64_t *row_begin);
 
 /* ------------------------------------------------------------------ plans
  * A plan holds the preprocessed schedule of A and every device buffer the
@@ -177,6 +182,17 @@ tcaspmm_status tcaspmm_plan_create(const tcaspmm_csr *A, int64_t N, tcaspmm_dtyp
 /* One process per GPU: a plan for rank's column block only, on `device`. */
 tcaspmm_status tcaspmm_plan_create_shard(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt, int rank,
                                          int world, int device, tcaspmm_plan **out);
+/* Row-split plans (tcaspmm_partition_rows): shard s holds rows [row_begin[s],
+ * row_begin[s+1]) of A and all N columns; at execute, dB[s] is the whole K x N
+ * B on its device and dC[s] the shard's (row_count x N) block of C. */
+tcaspmm_status tcaspmm_plan_create_rows(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt, int num_gpus,
+                                        const int *devices, tcaspmm_plan **out);
+/* One process per GPU: the plan of rank's row block only, on `device`. */
+tcaspmm_status tcaspmm_plan_create_rows_shard(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt, int rank,
+                                              int world, int device, tcaspmm_plan **out);
+/* Shard s's row block [row_begin, row_begin + row_count) (0 and M for column-split plans). */
+tcaspmm_status tcaspmm_plan_shard_rows(const tcaspmm_plan *plan, int shard, int64_t *row_begin,
+                                       int64_t *row_count);
 tcaspmm_status tcaspmm_plan_destroy(tcaspmm_plan *plan);
 tcaspmm_status tcaspmm_plan_get_stats(const tcaspmm_plan *plan, tcaspmm_plan_stats *out);
 /* Shard s of the plan: its device and its column block [col_begin, col_begin + col_count). */
@@ -192,6 +208,30 @@ tcaspmm_status tcaspmm_execute(tcaspmm_plan *plan, const void *const *dB, const 
 /* Single-shard convenience form of tcaspmm_execute. */
 tcaspmm_status tcaspmm_execute1(tcaspmm_plan *plan, const void *dB, int64_t ldb, float *dC,
                                 int64_t ldc, void *stream);
+/* Fused output epilogue (no counterpart in the reference, whose kernel ignores
+ * alpha/beta, src/our_spmm.cu:296-352): per shard,
+ *     C[r][c] = relu?( row_scale[r] * (A B)[r][c] + bias[c] )
+ * with row_scale (one float per row of the shard: M, or row_count for a
+ * row-split plan) and bias (col_count floats, the shard's column block) device
+ * arrays on the shard's device, NULL meaning 1 and 0, and C
+ * stored as out_dtype: TCASPMM_F32, TCASPMM_F16 or TCASPMM_BF16 (16-bit C halves
+ * the C bytes).  GraphSAGE mean aggregation is a pattern A with
+ * row_scale = 1/deg; a GCN layer's bias and ReLU fold in the same way. */
+typedef struct tcaspmm_epilogue {
+    const float *row_scale;
+    const float *bias;
+    int relu;
+    tcaspmm_dtype out_dtype;
+} tcaspmm_epilogue;
+
+/* tcaspmm_execute with an epilogue per shard (epilogues NULL = plain fp32 C);
+ * dC[s] has out_dtype elements and ldc[s] counts them. */
+tcaspmm_status tcaspmm_execute_ex(tcaspmm_plan *plan, const void *const *dB, const int64_t *ldb,
+                                  void *const *dC, const int64_t *ldc, void *const *streams,
+                                  const tcaspmm_epilogue *epilogues);
+/* Single-shard form of tcaspmm_execute_ex (ep NULL = plain fp32 C). */
+tcaspmm_status tcaspmm_execute1_ex(tcaspmm_plan *plan, const void *dB, int64_t ldb, void *dC,
+                                   int64_t ldc, void *stream, const tcaspmm_epilogue *ep);
 /* Wait for the plan's shards and report a device-side error (a bounded wait
  * that ran out in a tensor-core kernel) as TCASPMM_ERR_TIMEOUT. */
 tcaspmm_status tcaspmm_plan_sync_check(tcaspmm_plan *plan);

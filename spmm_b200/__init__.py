@@ -104,6 +104,10 @@ class _Stats(C.Structure):
         return {name: getattr(self, name) for name, _ in self._fields_}
 
 
+class _Epilogue(C.Structure):
+    _fields_ = [("row_scale", C.c_void_p), ("bias", C.c_void_p), ("relu", C.c_int), ("out_dtype", C.c_int)]
+
+
 _vp, _i64, _i32 = C.c_void_p, C.c_int64, C.c_int32
 _P = C.POINTER
 
@@ -134,11 +138,17 @@ _sig("tcaspmm_gen_skew", [_i64, _i64, _i64, C.c_double, C.c_uint64, _P(_CSR)])
 _sig("tcaspmm_partition_columns", [_i64, C.c_int, C.c_int, C.c_int, _P(_i64), _P(_i64)])
 _sig("tcaspmm_plan_create", [_P(_CSR), _i64, C.c_int, C.c_int, _P(C.c_int), _P(_vp)])
 _sig("tcaspmm_plan_create_shard", [_P(_CSR), _i64, C.c_int, C.c_int, C.c_int, C.c_int, _P(_vp)])
+_sig("tcaspmm_partition_rows", [_P(_CSR), C.c_int, _P(_i64)])
+_sig("tcaspmm_plan_create_rows", [_P(_CSR), _i64, C.c_int, C.c_int, _P(C.c_int), _P(_vp)])
+_sig("tcaspmm_plan_create_rows_shard", [_P(_CSR), _i64, C.c_int, C.c_int, C.c_int, C.c_int, _P(_vp)])
+_sig("tcaspmm_plan_shard_rows", [_vp, C.c_int, _P(_i64), _P(_i64)])
 _sig("tcaspmm_plan_destroy", [_vp])
 _sig("tcaspmm_plan_get_stats", [_vp, _P(_Stats)])
 _sig("tcaspmm_plan_shard", [_vp, C.c_int, _P(C.c_int), _P(_i64), _P(_i64)])
 _sig("tcaspmm_execute", [_vp, _P(_vp), _P(_i64), _P(_vp), _P(_i64), _P(_vp)])
 _sig("tcaspmm_execute1", [_vp, _vp, _i64, _vp, _i64, _vp])
+_sig("tcaspmm_execute_ex", [_vp, _P(_vp), _P(_i64), _P(_vp), _P(_i64), _P(_vp), _P(_Epilogue)])
+_sig("tcaspmm_execute1_ex", [_vp, _vp, _i64, _vp, _i64, _vp, _P(_Epilogue)])
 _sig("tcaspmm_plan_sync_check", [_vp])
 _sig("tcaspmm_plan_device_csr", [_vp, C.c_int, _P(_vp), _P(_vp), _P(_vp)])
 _sig("tcaspmm_schedule_coverage", [_P(_CSR), _i64, C.c_int, _vp, _vp, _P(_Stats)])
@@ -264,6 +274,14 @@ def gen_magnitude(M: int, K: int, sparsity: float, seed: int = 0) -> CSR:
     return _gen(lib.tcaspmm_gen_magnitude, M, K, sparsity, seed)
 
 
+def partition_rows(A: CSR, parts: int) -> np.ndarray:
+    """Row blocks of about equal cost (tcaspmm_partition_rows): parts + 1 boundaries."""
+    out = np.zeros(parts + 1, np.int64)
+    cA = A._c()
+    _check(lib.tcaspmm_partition_rows(C.byref(cA), parts, out.ctypes.data_as(_P(_i64))))
+    return out
+
+
 def gen_rmat(scale: int, edges: int, a=0.57, b=0.19, c=0.19, kind: str = "gcn", seed: int = 0) -> CSR:
     return _gen(lib.tcaspmm_gen_rmat, scale, edges, a, b, c, {"gcn": 0, "sage": 1}[kind], seed)
 
@@ -305,23 +323,56 @@ def _stream_handle(s) -> int:
     return int(s.cuda_stream)
 
 
+@dataclass
+class Epilogue:
+    """Fused output epilogue (tcaspmm_epilogue): C = relu?(row_scale[r] * (A @ B)[r, c] + bias[c]).
+
+    row_scale (M floats) and bias (one float per column of the shard's block) are
+    device tensors / pointers on the shard's device or None (1 and 0); out_dtype
+    is the type C is stored in: "f32", "f16" or "bf16".
+    """
+    row_scale: object = None
+    bias: object = None
+    relu: bool = False
+    out_dtype: object = "f32"
+
+    def _c(self) -> _Epilogue:
+        return _Epilogue(_ptr(self.row_scale) if self.row_scale is not None else None,
+                         _ptr(self.bias) if self.bias is not None else None, int(bool(self.relu)),
+                         int(as_dtype(self.out_dtype)))
+
+
 class Plan:
     """Preprocessed A on one or more GPUs (tcaspmm_plan_create / _create_shard)."""
 
     def __init__(self, A: CSR, N: int, dt="f16", num_gpus: int = 1, devices: Optional[Sequence[int]] = None,
-                 *, rank: Optional[int] = None, world: Optional[int] = None, device: Optional[int] = None):
+                 *, rank: Optional[int] = None, world: Optional[int] = None, device: Optional[int] = None,
+                 split: str = "columns"):
+        """split="columns": shards own column blocks of B and C (A replicated);
+        split="rows": shards own row blocks of A and C (B replicated)."""
+        if split not in ("columns", "rows"):
+            raise ValueError(f"split must be 'columns' or 'rows', not {split!r}")
         self._h = _vp()
         self.dt = as_dtype(dt)
+        self.split = split
         self.N, self.M, self.K, self.nnz = int(N), A.nrow, A.ncol, A.nnz
         cA = A._c()
         if rank is not None:
-            _check(lib.tcaspmm_plan_create_shard(C.byref(cA), N, int(self.dt), rank, world, device,
-                                                 C.byref(self._h)))
+            fn = lib.tcaspmm_plan_create_shard if split == "columns" else lib.tcaspmm_plan_create_rows_shard
+            _check(fn(C.byref(cA), N, int(self.dt), rank, world, device, C.byref(self._h)))
         else:
             devs = None
             if devices is not None:
                 devs = (C.c_int * len(devices))(*devices)
-            _check(lib.tcaspmm_plan_create(C.byref(cA), N, int(self.dt), num_gpus, devs, C.byref(self._h)))
+            fn = lib.tcaspmm_plan_create if split == "columns" else lib.tcaspmm_plan_create_rows
+            _check(fn(C.byref(cA), N, int(self.dt), num_gpus, devs, C.byref(self._h)))
+        # Nonzeros per shard (row blocks hold part of A).
+        if split == "rows":
+            rb = partition_rows(A, world if rank is not None else num_gpus)
+            parts = [rank] if rank is not None else range(num_gpus)
+            self._shard_nnz = [int(A.row_ptr[rb[i + 1]] - A.row_ptr[rb[i]]) for i in parts]
+        else:
+            self._shard_nnz = [A.nnz] * (1 if rank is not None else num_gpus)
 
     def close(self) -> None:
         if self._h:
@@ -351,13 +402,25 @@ class Plan:
         return int(self.stats["num_shards"])
 
     def shard(self, s: int):
+        """(device, col_begin, col_count) of shard s."""
         dev, b, c = C.c_int(), _i64(), _i64()
         _check(lib.tcaspmm_plan_shard(self._h, s, C.byref(dev), C.byref(b), C.byref(c)))
         return dev.value, b.value, c.value
 
+    def shard_nnz(self, s: int) -> int:
+        return self._shard_nnz[s]
+
+    def shard_rows(self, s: int):
+        """(row_begin, row_count) of shard s (0, M for column-split plans)."""
+        b, c = _i64(), _i64()
+        _check(lib.tcaspmm_plan_shard_rows(self._h, s, C.byref(b), C.byref(c)))
+        return b.value, c.value
+
     def execute(self, B: Sequence, Cs: Sequence, ldb: Optional[Sequence[int]] = None,
-                ldc: Optional[Sequence[int]] = None, streams: Optional[Sequence] = None) -> None:
-        """Launch C[s] = A @ B[s] for every shard s (device tensors or raw pointers)."""
+                ldc: Optional[Sequence[int]] = None, streams: Optional[Sequence] = None,
+                epilogues: Optional[Sequence[Epilogue]] = None) -> None:
+        """Launch C[s] = A @ B[s] for every shard s (device tensors or raw pointers),
+        through epilogues[s] when given."""
         n = len(B)
         ldb = ldb or [int(b.stride(0)) for b in B]
         ldc = ldc or [int(c.stride(0)) for c in Cs]
@@ -366,12 +429,22 @@ class Plan:
         lb = (_i64 * n)(*ldb)
         lc = (_i64 * n)(*ldc)
         st = (_vp * n)(*[_stream_handle(s) for s in (streams or [None] * n)])
-        _check(lib.tcaspmm_execute(self._h, pb, lb, pc, lc, st))
+        if epilogues is None:
+            _check(lib.tcaspmm_execute(self._h, pb, lb, pc, lc, st))
+        else:
+            eps = (_Epilogue * n)(*[e._c() for e in epilogues])
+            _check(lib.tcaspmm_execute_ex(self._h, pb, lb, pc, lc, st, eps))
 
-    def execute1(self, B, Cout, stream=None, ldb: Optional[int] = None, ldc: Optional[int] = None) -> None:
+    def execute1(self, B, Cout, stream=None, ldb: Optional[int] = None, ldc: Optional[int] = None,
+                 epilogue: Optional[Epilogue] = None) -> None:
         lb = ldb if ldb is not None else int(B.stride(0))
         lc = ldc if ldc is not None else int(Cout.stride(0))
-        _check(lib.tcaspmm_execute1(self._h, _ptr(B), lb, _ptr(Cout), lc, _stream_handle(stream)))
+        if epilogue is None:
+            _check(lib.tcaspmm_execute1(self._h, _ptr(B), lb, _ptr(Cout), lc, _stream_handle(stream)))
+        else:
+            ep = epilogue._c()
+            _check(lib.tcaspmm_execute1_ex(self._h, _ptr(B), lb, _ptr(Cout), lc, _stream_handle(stream),
+                                           C.byref(ep)))
 
     def sync_check(self) -> None:
         _check(lib.tcaspmm_plan_sync_check(self._h))
@@ -448,7 +521,9 @@ def cusparse_spmm(plan: Plan, B, Cout, warmup: int = 10, iters: int = 10, stream
     rp, col, val = plan.device_csr(shard)
     ms = C.c_double()
     _, _, ncols = plan.shard(shard)
-    _check(baselines().tcaspmm_cusparse_spmm(rp, col, val, plan.M, plan.K, plan.nnz, _ptr(B), int(B.stride(0)),
+    _, rows = plan.shard_rows(shard)
+    _check(baselines().tcaspmm_cusparse_spmm(rp, col, val, rows, plan.K, plan.shard_nnz(shard), _ptr(B),
+                                             int(B.stride(0)),
                                              _ptr(Cout), int(Cout.stride(0)), ncols, int(plan.dt), warmup, iters,
                                              _stream_handle(stream), C.byref(ms)))
     return ms.value

@@ -200,4 +200,24 @@ tcaspmm_status tcaspmm_partition_columns(int64_t N, tcaspmm_dtype dt, int world,
     return TCASPMM_OK;
 }
 
+tcaspmm_status tcaspmm_partition_rows(const tcaspmm_csr *A, int parts, int64_t *row_begin)
+{
+    if (!A || parts < 1 || !row_begin) return fail(TCASPMM_ERR_INVALID_ARG, "partition_rows: bad arguments");
+    tcaspmm_status s = tcaspmm_csr_validate(A);
+    if (s != TCASPMM_OK) return s;
+    // Cost of rows [0, r) = row_ptr[r] + 2 r; block i starts at the first row
+    // whose prefix cost reaches i / parts of the total.
+    const int64_t M = A->nrow;
+    const int64_t total = A->row_ptr[M] + 2 * M;
+    row_begin[0] = 0;
+    int64_t r = 0;
+    for (int i = 1; i < parts; i++) {
+        const int64_t target = (int64_t)((__int128)total * i / parts);
+        while (r < M && A->row_ptr[r] + 2 * r < target) r++;
+        row_begin[i] = r;
+    }
+    row_begin[parts] = M;
+    return TCASPMM_OK;
+}
+
 }  // extern "C"

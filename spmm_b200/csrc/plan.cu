@@ -17,7 +17,7 @@
 
 #include "internal.h"
 #include "plan.h"
-#include "residue.cuh"
+#include "residue_dispatch.cuh"
 
 using namespace tca;
 
@@ -74,13 +74,29 @@ std::vector<uint16_t> to_16bit(const float *v, int64_t n, tcaspmm_dtype dt)
     return out;
 }
 
-tcaspmm_status build_shard(const tcaspmm_csr &A, tcaspmm_dtype dt, int device, int64_t col_begin,
-                           int64_t ncols, Shard *sh, double *prep_ms)
+tcaspmm_status build_shard(const tcaspmm_csr &Afull, tcaspmm_dtype dt, int device, int64_t col_begin,
+                           int64_t ncols, int64_t row_begin, int64_t nrows, Shard *sh, double *prep_ms)
 {
     sh->device = device;
     sh->col_begin = col_begin;
     sh->ncols = ncols;
-    sh->K = A.ncol;
+    sh->row_begin = row_begin;
+    sh->nrows = nrows;
+    sh->K = Afull.ncol;
+    // A row block is the CSR view of rows [row_begin, row_begin + nrows) with
+    // rebased offsets.
+    std::vector<int64_t> sub_rp;
+    tcaspmm_csr A = Afull;
+    if (row_begin != 0 || nrows != Afull.nrow) {
+        const int64_t base = Afull.row_ptr[row_begin];
+        sub_rp.resize((size_t)nrows + 1);
+        for (int64_t i = 0; i <= nrows; i++) sub_rp[i] = Afull.row_ptr[row_begin + i] - base;
+        A.nrow = nrows;
+        A.nnz = sub_rp[nrows];
+        A.row_ptr = sub_rp.data();
+        A.col_idx = Afull.col_idx + base;
+        A.val = Afull.val ? Afull.val + base : nullptr;
+    }
     DeviceGuard g(device);
     int nsm = 148;
     cudaError_t e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device);
@@ -143,39 +159,10 @@ tcaspmm_status build_shard(const tcaspmm_csr &A, tcaspmm_dtype dt, int device, i
     return TCASPMM_OK;
 }
 
-template <typename T, int VEC, int G>
-void launch_res(const ResidueParams &p, int total_warps, cudaStream_t st)
-{
-    const int blocks = (total_warps + 7) / 8;
-    residue_kernel<T, VEC, G, 8><<<blocks, 256, 0, st>>>(p);
-}
-
-template <typename T, int VEC>
-void launch_res_g(int G, const ResidueParams &p, int total_warps, cudaStream_t st)
-{
-    switch (G) {
-    case 1: launch_res<T, VEC, 1>(p, total_warps, st); break;
-    case 2: launch_res<T, VEC, 2>(p, total_warps, st); break;
-    case 4: launch_res<T, VEC, 4>(p, total_warps, st); break;
-    case 8: launch_res<T, VEC, 8>(p, total_warps, st); break;
-    case 16: launch_res<T, VEC, 16>(p, total_warps, st); break;
-    default: launch_res<T, VEC, 32>(p, total_warps, st); break;
-    }
-}
-
-template <typename T>
-void launch_res_t(bool vec, int G, const ResidueParams &p, int total_warps, cudaStream_t st)
-{
-    if (vec)
-        launch_res_g<T, 16 / sizeof(T)>(G, p, total_warps, st);
-    else
-        launch_res_g<T, 1>(G, p, total_warps, st);
-}
-
 }  // namespace
 
-tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB, int64_t ldb, float *dC,
-                              int64_t ldc, cudaStream_t st, const Int2 *ranges, int n_ranges)
+tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB, int64_t ldb, void *dC, int64_t ldc,
+                              const Epilogue *ep, cudaStream_t st, const Int2 *ranges, int n_ranges)
 {
     const bool whole_rows = ranges != nullptr;
     const int n_segs = whole_rows ? 0 : sh.n_segs;
@@ -186,9 +173,11 @@ tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB,
     const int total = n_segs + n_ranges;
     if (total == 0 || sh.ncols == 0) return TCASPMM_OK;
     const int elem = dtype_size(dt);
-    // 16-byte vector path needs 16-byte aligned B and C rows.
+    // 16-byte vector path needs 16-byte aligned B rows and aligned C rows
+    // (16 bytes for fp32 C; 8 or 16 bytes for 16-bit C, VEC = 4 or 8).
+    const int out_elem = ep ? ep->out_size() : 4;
     const bool vec = ((uintptr_t)dB % 16 == 0) && ((ldb * elem) % 16 == 0) && ((uintptr_t)dC % 16 == 0) &&
-                     (ldc % 4 == 0) && (sh.ncols % (16 / elem) == 0);
+                     ((ldc * out_elem) % 16 == 0) && (sh.ncols % (16 / elem) == 0);
     int G, VEC;
     residue_shape(sh.ncols, dt, vec, &G, &VEC);
     // The row ranges were cut for the vector shape; the scalar path uses the
@@ -199,7 +188,7 @@ tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB,
     p.val = sh.val;
     p.B = dB;
     p.ldb = ldb;
-    p.C = dC;
+    p.C = static_cast<float *>(dC);
     p.ldc = ldc;
     p.ncols = (int)sh.ncols;
     p.ranges = (const int2 *)ranges;
@@ -210,12 +199,13 @@ tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB,
     p.partials = sh.partials;
     p.pstride = sh.pstride;
     p.counters = sh.counters;
-    if (dt == TCASPMM_F32)
-        launch_res_t<float>(vec, G, p, total, st);
-    else if (dt == TCASPMM_F16)
-        launch_res_t<__half>(vec, G, p, total, st);
-    else
-        launch_res_t<__nv_bfloat16>(vec, G, p, total, st);
+    p.ep = EpiParams{nullptr, nullptr, 0, 0};
+    if (ep) {
+        p.ep = EpiParams{ep->row_scale, ep->bias, ep->relu, ep->out};
+        launch_residue_epi(dt, vec, G, p, total, st);
+    } else {
+        launch_res_dt<false>(dt, vec, G, p, total, st);
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "residue kernel launch");
     return TCASPMM_OK;
@@ -242,10 +232,15 @@ struct tcaspmm_plan {
     }
 };
 
+// Shards: column blocks (begins/counts) of all rows, or, with row blocks given
+// (row_begins/row_counts), row blocks of all N columns.
 static tcaspmm_status create_common(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt,
                                     const std::vector<int> &devices, const std::vector<int64_t> &begins,
-                                    const std::vector<int64_t> &counts, tcaspmm_plan **out)
+                                    const std::vector<int64_t> &counts, tcaspmm_plan **out,
+                                    const std::vector<int64_t> &row_begins = {},
+                                    const std::vector<int64_t> &row_counts = {})
 {
+    const bool split_rows = !row_begins.empty();
     auto t0 = std::chrono::steady_clock::now();
     std::unique_ptr<tcaspmm_plan> P(new tcaspmm_plan());
     P->M = A->nrow;
@@ -256,7 +251,8 @@ static tcaspmm_status create_common(const tcaspmm_csr *A, int64_t N, tcaspmm_dty
     double prep = 0.0;
     for (size_t i = 0; i < devices.size(); i++) {
         P->shards.emplace_back(new Shard());
-        tcaspmm_status s = build_shard(*A, dt, devices[i], begins[i], counts[i], P->shards.back().get(), &prep);
+        tcaspmm_status s = build_shard(*A, dt, devices[i], begins[i], counts[i], split_rows ? row_begins[i] : 0,
+                                       split_rows ? row_counts[i] : A->nrow, P->shards.back().get(), &prep);
         if (s != TCASPMM_OK) return s;
     }
     const double total = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
@@ -268,16 +264,21 @@ static tcaspmm_status create_common(const tcaspmm_csr *A, int64_t N, tcaspmm_dty
     st.ncols_total = N;
     st.num_shards = (int32_t)P->shards.size();
     st.window_rows = S.tc.R;
-    st.tc_windows = (int64_t)S.tc.windows.size();
-    st.tc_tiles = S.tc.KT ? (int64_t)S.tc.tile_cols.size() / S.tc.KT : 0;
-    st.tc_nnz = S.tc.nnz;
-    st.residue_nnz = S.res.nnz;
-    st.residue_row_warps = (int64_t)S.res.ranges.size();
-    st.residue_segments = (int64_t)S.res.segs.size();
-    st.long_rows = (int64_t)S.res.longs.size();
+    // Column shards share one schedule (shard 0 speaks for all); row shards
+    // add up.
+    for (size_t i = 0; i < (split_rows ? P->shards.size() : 1); i++) {
+        const Schedule &Si = P->shards[i]->sched;
+        st.tc_windows += (int64_t)Si.tc.windows.size();
+        st.tc_tiles += Si.tc.KT ? (int64_t)Si.tc.tile_cols.size() / Si.tc.KT : 0;
+        st.tc_nnz += Si.tc.nnz;
+        st.residue_nnz += Si.res.nnz;
+        st.residue_row_warps += (int64_t)Si.res.ranges.size();
+        st.residue_segments += (int64_t)Si.res.segs.size();
+        st.long_rows += (int64_t)Si.res.longs.size();
+        st.device_bytes = std::max<int64_t>(st.device_bytes, P->shards[i]->bytes);
+    }
     st.preprocess_ms = prep;
     st.upload_ms = total - prep;
-    st.device_bytes = P->shards[0]->bytes;
     st.algorithmic_bytes = algorithmic_bytes(A->nrow, A->ncol, A->nnz, N, dt);
     for (auto &sh : P->shards) sh->sched = Schedule();  // host copies are on the device now
     *out = P.release();
@@ -337,6 +338,66 @@ tcaspmm_status tcaspmm_plan_create_shard(const tcaspmm_csr *A, int64_t N, tcaspm
     return create_common(A, N, dt, {device}, {b}, {c}, out);
 }
 
+static tcaspmm_status device_count_check(int n, const int *devices, std::vector<int> *devs)
+{
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return fail(TCASPMM_ERR_NO_DEVICE, "no CUDA device");
+    }
+    devs->resize(n);
+    for (int i = 0; i < n; i++) {
+        (*devs)[i] = devices ? devices[i] : i;
+        if ((*devs)[i] < 0 || (*devs)[i] >= ndev)
+            return fail(TCASPMM_ERR_NO_DEVICE, "device %d requested, %d present", (*devs)[i], ndev);
+    }
+    return TCASPMM_OK;
+}
+
+tcaspmm_status tcaspmm_plan_create_rows(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt, int num_gpus,
+                                        const int *devices, tcaspmm_plan **out)
+{
+    clear_error();
+    tcaspmm_status s = check_inputs(A, N, dt, out);
+    if (s != TCASPMM_OK) return s;
+    if (num_gpus < 1) return fail(TCASPMM_ERR_INVALID_ARG, "num_gpus=%d", num_gpus);
+    std::vector<int> devs;
+    if ((s = device_count_check(num_gpus, devices, &devs)) != TCASPMM_OK) return s;
+    std::vector<int64_t> rb(num_gpus + 1);
+    if ((s = tcaspmm_partition_rows(A, num_gpus, rb.data())) != TCASPMM_OK) return s;
+    std::vector<int64_t> b(num_gpus, 0), c(num_gpus, N), r0(num_gpus), rc(num_gpus);
+    for (int i = 0; i < num_gpus; i++) {
+        r0[i] = rb[i];
+        rc[i] = rb[i + 1] - rb[i];
+    }
+    return create_common(A, N, dt, devs, b, c, out, r0, rc);
+}
+
+tcaspmm_status tcaspmm_plan_create_rows_shard(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt, int rank,
+                                              int world, int device, tcaspmm_plan **out)
+{
+    clear_error();
+    tcaspmm_status s = check_inputs(A, N, dt, out);
+    if (s != TCASPMM_OK) return s;
+    if (world < 1 || rank < 0 || rank >= world)
+        return fail(TCASPMM_ERR_INVALID_ARG, "plan_create_rows_shard: rank %d of %d", rank, world);
+    std::vector<int> devs;
+    if ((s = device_count_check(1, &device, &devs)) != TCASPMM_OK) return s;
+    std::vector<int64_t> rb(world + 1);
+    if ((s = tcaspmm_partition_rows(A, world, rb.data())) != TCASPMM_OK) return s;
+    return create_common(A, N, dt, devs, {0}, {N}, out, {rb[rank]}, {rb[rank + 1] - rb[rank]});
+}
+
+tcaspmm_status tcaspmm_plan_shard_rows(const tcaspmm_plan *plan, int shard, int64_t *row_begin, int64_t *row_count)
+{
+    if (!plan || shard < 0 || shard >= (int)plan->shards.size())
+        return fail(TCASPMM_ERR_INVALID_ARG, "plan_shard_rows: bad shard %d", shard);
+    const Shard &s = *plan->shards[shard];
+    if (row_begin) *row_begin = s.row_begin;
+    if (row_count) *row_count = s.nrows;
+    return TCASPMM_OK;
+}
+
 tcaspmm_status tcaspmm_plan_destroy(tcaspmm_plan *plan)
 {
     delete plan;
@@ -362,34 +423,60 @@ tcaspmm_status tcaspmm_plan_shard(const tcaspmm_plan *plan, int shard, int *devi
     return TCASPMM_OK;
 }
 
-tcaspmm_status tcaspmm_execute(tcaspmm_plan *plan, const void *const *dB, const int64_t *ldb, float *const *dC,
-                               const int64_t *ldc, void *const *streams)
+tcaspmm_status tcaspmm_execute_ex(tcaspmm_plan *plan, const void *const *dB, const int64_t *ldb, void *const *dC,
+                                  const int64_t *ldc, void *const *streams, const tcaspmm_epilogue *epilogues)
 {
     if (!plan || !dB || !ldb || !dC || !ldc) return fail(TCASPMM_ERR_INVALID_ARG, "execute: NULL argument");
     for (size_t i = 0; i < plan->shards.size(); i++) {
         const Shard &sh = *plan->shards[i];
-        if (sh.ncols == 0 || plan->M == 0) continue;
+        if (sh.ncols == 0 || sh.nrows == 0) continue;
         if (ldb[i] < sh.ncols || ldc[i] < sh.ncols)
             return fail(TCASPMM_ERR_INVALID_ARG, "execute: shard %zu ldb=%lld ldc=%lld below %lld columns", i,
                         (long long)ldb[i], (long long)ldc[i], (long long)sh.ncols);
         if (!dC[i] || (!dB[i] && plan->K > 0))
             return fail(TCASPMM_ERR_INVALID_ARG, "execute: shard %zu has a NULL B or C", i);
+        Epilogue ep;
+        if (epilogues) {
+            const tcaspmm_epilogue &e = epilogues[i];
+            ep.row_scale = e.row_scale;
+            ep.bias = e.bias;
+            ep.relu = e.relu != 0;
+            switch (e.out_dtype) {
+            case TCASPMM_F32: ep.out = 0; break;
+            case TCASPMM_F16: ep.out = 1; break;
+            case TCASPMM_BF16: ep.out = 2; break;
+            default: return fail(TCASPMM_ERR_INVALID_ARG, "execute: shard %zu has an unknown output dtype", i);
+            }
+        }
         cudaStream_t st = streams ? (cudaStream_t)streams[i] : (cudaStream_t)0;
         DeviceGuard g(sh.device);
-        tcaspmm_status s = launch_tc(sh, plan->dt, dB[i], ldb[i], dC[i], ldc[i], st);
+        const Epilogue *epp = epilogues ? &ep : nullptr;
+        tcaspmm_status s = launch_tc(sh, plan->dt, dB[i], ldb[i], dC[i], ldc[i], epp, st);
         if (s != TCASPMM_OK) return s;
-        s = launch_residue(sh, plan->dt, dB[i], ldb[i], dC[i], ldc[i], st);
+        s = launch_residue(sh, plan->dt, dB[i], ldb[i], dC[i], ldc[i], epp, st);
         if (s != TCASPMM_OK) return s;
     }
     return TCASPMM_OK;
 }
 
-tcaspmm_status tcaspmm_execute1(tcaspmm_plan *plan, const void *dB, int64_t ldb, float *dC, int64_t ldc, void *stream)
+tcaspmm_status tcaspmm_execute(tcaspmm_plan *plan, const void *const *dB, const int64_t *ldb, float *const *dC,
+                               const int64_t *ldc, void *const *streams)
+{
+    return tcaspmm_execute_ex(plan, dB, ldb, reinterpret_cast<void *const *>(dC), ldc, streams, nullptr);
+}
+
+tcaspmm_status tcaspmm_execute1_ex(tcaspmm_plan *plan, const void *dB, int64_t ldb, void *dC, int64_t ldc,
+                                   void *stream, const tcaspmm_epilogue *ep)
 {
     if (!plan) return fail(TCASPMM_ERR_INVALID_ARG, "execute1: plan is NULL");
     if (plan->shards.size() != 1)
         return fail(TCASPMM_ERR_INVALID_ARG, "execute1: plan has %zu shards", plan->shards.size());
-    return tcaspmm_execute(plan, &dB, &ldb, &dC, &ldc, &stream);
+    return tcaspmm_execute_ex(plan, &dB, &ldb, &dC, &ldc, &stream, ep);
+}
+
+tcaspmm_status tcaspmm_execute1(tcaspmm_plan *plan, const void *dB, int64_t ldb, float *dC, int64_t ldc, void *stream)
+{
+    return tcaspmm_execute1_ex(plan, dB, ldb, dC, ldc, stream, nullptr);
 }
 
 tcaspmm_status tcaspmm_plan_sync_check(tcaspmm_plan *plan)

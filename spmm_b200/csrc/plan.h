@@ -11,7 +11,8 @@ namespace tca {
 
 struct Shard {
     int device = 0;
-    int64_t col_begin = 0, ncols = 0;
+    int64_t col_begin = 0, ncols = 0;  // column block of B and C
+    int64_t row_begin = 0, nrows = 0;  // row block of A and C (all rows unless row-split)
     int64_t K = 0;  // rows of B
     Schedule sched;  // host schedule; large arrays are released after upload
     std::vector<void *> allocs;
@@ -35,15 +36,14 @@ struct Shard {
     // Tensor-core windows.
     int n_windows = 0;
     int num_sms = 148;
-    Int4 *tc_windows = nullptr;   // {first row, first tile, tiles, rows}
-    int32_t *tc_order = nullptr;  // windows by decreasing tile count
+    int tc_ctas_per_sm = 1;       // resident tc-kernel CTAs per SM (persistent grid)
+    Int4 *tc_windows = nullptr;   // {first row, first tile, tiles, rows}, by decreasing tile count
     int32_t *tc_cols = nullptr;   // KT B-row indices per tile
     void *tc_vals = nullptr;      // R x KT values per tile, shared-memory image
     Int2 *tc_fallback = nullptr;  // one row range per window (unaligned B: CUDA cores)
-    bool tc_tma = true;           // TMA producer (else 16-byte cp.async gathers)
     // Tensor maps over the last B block launched (rebuilt when B or ldb change);
-    // opaque storage for two 128-byte CUtensorMap objects.
-    alignas(64) mutable unsigned char maps[256] = {};
+    // opaque storage for three 128-byte CUtensorMap objects.
+    alignas(64) mutable unsigned char maps[384] = {};
     mutable bool maps_valid = false;
     mutable const void *maps_ptr = nullptr;
     mutable int64_t maps_ldb = 0;
@@ -51,17 +51,33 @@ struct Shard {
     int *err = nullptr;  // device error word (bounded waits that ran out)
 };
 
+// Fused output epilogue of one launch (tcaspmm_epilogue after validation):
+// C = relu?(row_scale[r] * (A B)[r][c] + bias[c]) stored as fp32 (out 0), fp16
+// (1) or bf16 (2).
+struct Epilogue {
+    const float *row_scale = nullptr;
+    const float *bias = nullptr;
+    int relu = 0;
+    int out = 0;
+    int out_size() const { return out == 0 ? 4 : 2; }
+};
+
+struct ResidueParams;
+
 tcaspmm_status cuda_fail(cudaError_t e, const char *what);
 void free_shard(Shard &sh);
 
 // Tensor-core path (tc.cu).
 bool tc_supported();
 tcaspmm_status tc_upload(const tcaspmm_csr &A, tcaspmm_dtype dt, Shard *sh);
-tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int64_t ldb, float *dC, int64_t ldc,
-                         cudaStream_t st);
+// `ep` NULL: plain fp32 C.  ldc counts elements of the output type.
+tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int64_t ldb, void *dC, int64_t ldc,
+                         const Epilogue *ep, cudaStream_t st);
 // CUDA-core residue kernel over the shard's row ranges and segments, or, with
 // `ranges` given, over those ranges only (whole rows of any length, no segments).
-tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB, int64_t ldb, float *dC,
-                              int64_t ldc, cudaStream_t st, const Int2 *ranges = nullptr, int n_ranges = 0);
+tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB, int64_t ldb, void *dC, int64_t ldc,
+                              const Epilogue *ep, cudaStream_t st, const Int2 *ranges = nullptr, int n_ranges = 0);
+// The epilogue instantiations of the residue kernel (residue_epi.cu).
+void launch_residue_epi(tcaspmm_dtype dt, bool vec, int G, const ResidueParams &p, int total_warps, cudaStream_t st);
 
 }  // namespace tca

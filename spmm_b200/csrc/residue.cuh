@@ -24,6 +24,17 @@
 
 namespace tca {
 
+// Fused output epilogue, applied where a C element is written:
+//   C[r][c] = relu?( row_scale[r] * (A B)[r][c] + bias[c] )  stored as fp32, fp16 or bf16.
+// row_scale / bias are device arrays (NULL = 1 / 0); c is the column within the
+// launch's column block.
+struct EpiParams {
+    const float *__restrict__ row_scale;
+    const float *__restrict__ bias;
+    int relu;
+    int out;  // 0 fp32, 1 fp16, 2 bf16
+};
+
 struct ResidueParams {
     const int32_t *__restrict__ row_ptr;
     const int32_t *__restrict__ col;
@@ -41,6 +52,7 @@ struct ResidueParams {
     float *partials;                 // n_segs x pstride
     int pstride;
     unsigned int *counters;          // one per long row, zero between launches
+    EpiParams ep;                    // used by the EPI instantiations only
 };
 
 template <typename T> __device__ __forceinline__ float to_f(T x);
@@ -141,6 +153,56 @@ __device__ __forceinline__ void add_l2(const float *c, float (&a)[VEC])
     }
 }
 
+// Epilogue then store of VEC outputs of row r at column c0 of the block.
+template <int VEC>
+__device__ __forceinline__ void store_epi(const ResidueParams &p, long long r, int c0, float (&a)[VEC])
+{
+    const EpiParams &ep = p.ep;
+    const float s = ep.row_scale ? __ldg(ep.row_scale + r) : 1.0f;
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+        float x = a[k] * s;
+        if (ep.bias) x += __ldg(ep.bias + c0 + k);
+        a[k] = ep.relu ? fmaxf(x, 0.0f) : x;
+    }
+    if (ep.out == 0) {
+        store_c<VEC>(p.C + r * p.ldc + c0, a);
+        return;
+    }
+    // 16-bit outputs: VEC = 1 one element, 4 -> 8 bytes, 8 -> 16 bytes.
+    uint32_t h[(VEC + 1) / 2];
+    if constexpr (VEC == 1) {
+        uint16_t *c = reinterpret_cast<uint16_t *>(p.C) + r * p.ldc + c0;
+        *c = ep.out == 1 ? __half_as_ushort(__float2half_rn(a[0])) : __bfloat16_as_ushort(__float2bfloat16_rn(a[0]));
+    } else {
+#pragma unroll
+        for (int k = 0; k < VEC / 2; ++k) {
+            if (ep.out == 1) {
+                const __half2 v = __floats2half2_rn(a[2 * k], a[2 * k + 1]);
+                h[k] = *reinterpret_cast<const uint32_t *>(&v);
+            } else {
+                const __nv_bfloat162 v = __floats2bfloat162_rn(a[2 * k], a[2 * k + 1]);
+                h[k] = *reinterpret_cast<const uint32_t *>(&v);
+            }
+        }
+        uint16_t *c = reinterpret_cast<uint16_t *>(p.C) + r * p.ldc + c0;
+        if constexpr (VEC == 4)
+            __stcs(reinterpret_cast<uint2 *>(c), make_uint2(h[0], h[1]));
+        else
+            __stcs(reinterpret_cast<uint4 *>(c), make_uint4(h[0], h[1], h[2], h[3]));
+    }
+}
+
+// The store of a finished output slice: plain fp32, or through the epilogue.
+template <int VEC, bool EPI>
+__device__ __forceinline__ void emit(const ResidueParams &p, long long r, int c0, float (&a)[VEC])
+{
+    if constexpr (EPI)
+        store_epi<VEC>(p, r, c0, a);
+    else
+        store_c<VEC>(p.C + r * p.ldc + c0, a);
+}
+
 // acc += sum_{j in [b, e)} val[j] * B[col[j]][c0 .. c0+VEC): full chunks of U
 // without predicates (U indices, U independent B loads, U FMAs), then the
 // remainder one nonzero at a time.
@@ -175,13 +237,12 @@ __device__ __forceinline__ void accumulate_lean(const ResidueParams &p, int b, c
 // run without predicates (U indices, U B loads, U FMAs with a row-end check),
 // the remainder one nonzero at a time; each row is written when the stream
 // passes its end, trailing empty rows too.
-template <typename T, int VEC, int U>
+template <typename T, int VEC, int U, bool EPI>
 __device__ __forceinline__ void stream_lean(const ResidueParams &p, int r_lo, int r_hi, int c0)
 {
     if (r_lo >= r_hi) return;
     const T *__restrict__ B = static_cast<const T *>(p.B) + c0;
     const T *__restrict__ val = static_cast<const T *>(p.val);
-    float *__restrict__ C = p.C + c0;
     int r = r_lo;
     int e = __ldg(p.row_ptr + r + 1);
     int j = __ldg(p.row_ptr + r_lo);
@@ -191,7 +252,7 @@ __device__ __forceinline__ void stream_lean(const ResidueParams &p, int r_lo, in
     for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
     auto pass_row_ends = [&](int jj) {
         while (jj >= e) {
-            store_c<VEC>(C + (long long)r * p.ldc, acc);
+            emit<VEC, EPI>(p, r, c0, acc);
 #pragma unroll
             for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
             ++r;
@@ -223,7 +284,7 @@ __device__ __forceinline__ void stream_lean(const ResidueParams &p, int r_lo, in
         fma_raw<T, VEC>(v, rb, acc);
     }
     for (; r < r_hi; ++r) {
-        store_c<VEC>(C + (long long)r * p.ldc, acc);
+        emit<VEC, EPI>(p, r, c0, acc);
 #pragma unroll
         for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
     }
@@ -244,9 +305,10 @@ __device__ __forceinline__ int first_row_at(const int32_t *row_ptr, int lo, int 
 
 // 256 threads, register budget for 4 resident blocks per SM (64 registers):
 // measured faster than 40 registers / 6 blocks and than 80 / 3 on GCN, SAGE and
-// the skew config.
-template <typename T, int VEC, int G, int U>
-__global__ void __launch_bounds__(256, 4) residue_kernel(const ResidueParams p)
+// the skew config.  The epilogue instantiations get 3 blocks (80 registers) so
+// the epilogue's live values do not spill the nonzero stream.
+template <typename T, int VEC, int G, int U, bool EPI>
+__global__ void __launch_bounds__(256, EPI ? 3 : 4) residue_kernel(const ResidueParams p)
 {
     constexpr int P = 32 / G;
     constexpr int CPP = G * VEC;  // columns per pass
@@ -296,7 +358,7 @@ __global__ void __launch_bounds__(256, 4) residue_kernel(const ResidueParams p)
                 for (int off = G; off < 32; off <<= 1)
 #pragma unroll
                     for (int k = 0; k < VEC; ++k) acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], off);
-                if (sub == 0 && c0 < p.ncols) store_c<VEC>(p.C + (long long)L.x * p.ldc + c0, acc);
+                if (sub == 0 && c0 < p.ncols) emit<VEC, EPI>(p, L.x, c0, acc);
             }
             if (lane == 0) p.counters[s.w] = 0u;  // ready for the next launch
         }
@@ -322,7 +384,7 @@ __global__ void __launch_bounds__(256, 4) residue_kernel(const ResidueParams p)
     for (int pass = 0; pass < npass; ++pass) {
         const int c0 = pass * CPP + gl * VEC;
         if (c0 >= p.ncols) break;
-        stream_lean<T, VEC, U>(p, r_lo, r_hi, c0);
+        stream_lean<T, VEC, U, EPI>(p, r_lo, r_hi, c0);
     }
 }
 

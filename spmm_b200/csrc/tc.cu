@@ -14,24 +14,23 @@
 //
 // Shared-memory operands.  B = value tile, K-major, no swizzle: R rows x 16 k,
 // core matrix = 8 rows x 8 k, k step LBO = 128 B, rows step SBO = 256 B; the
-// host stores each tile's values in exactly this image.  A = B panel (16
-// gathered B rows x 128 columns), MN-major, filled by one of two producers:
-//   TMA producer (default): 128-byte-swizzled atoms of 8 k-rows x 64 columns;
-//       the two 64-column halves are LBO = 2 KB apart, the two groups of 8
-//       k-rows SBO = 1 KB apart.  One lane issues, per tile, either 2 TMA tile
-//       loads of a 64 x 16 box (when the tile's 16 B rows are consecutive, as in
-//       dense windows) or 8 tile::gather4 loads of 4 rows each, plus one 1 KB
-//       cp.async.bulk of the value tile; the 2-D tensor map over B writes the
-//       swizzle and zero-fills columns past N.
-//   cp.async producer: no swizzle, core matrix = 8 k-rows x 8 columns (128 B);
-//       columns step SBO = 256 B, k step LBO = 128 B; 4 warps of 16-byte
-//       cp.async gathers.
+// host stores each tile's values in exactly this image.  A = B panel (gathered
+// B rows x 128 columns), MN-major, 128-byte swizzled atoms of 8 k-rows x 64
+// columns written by TMA.  One pipeline stage holds TPS = 4 tiles (K = 64): per
+// 64-column half, 8 atoms of 1 KB, so a tile's descriptor has SBO = 1 KB
+// (next 8 k-rows) and LBO = 8 KB (next column half).  One lane fills a stage
+// with, per column half, a single 64 x 64 TMA box when the stage's 64 B rows
+// are consecutive (dense windows), else per tile a 64 x 16 box (16 consecutive
+// rows) or four tile::gather4 loads of 4 rows, plus one cp.async.bulk of the
+// stage's value tiles; the 2-D tensor maps over B write the swizzle and
+// zero-fill columns past N.  The MMA thread issues the stage's 4 MMAs and one
+// commit, so the barrier round trips are paid per K = 64, not per K = 16.
 //
 // Warp roles: warps 0-3 epilogue (tcgen05.ld of TMEM lanes 32w..32w+31 ->
 // coalesced fp32 C rows), warp 4 TMEM allocation + MMA issue (one thread),
-// warp 5 (TMA) or warps 5-8 (cp.async) producers on a 16-stage mbarrier ring,
-// B-row indices staged in shared memory by coalesced warp loads.  Two TMEM
-// accumulators let the epilogue of one unit overlap the MMAs of the next.
+// warp 5 producer on an 8-stage mbarrier ring, B-row indices staged in shared
+// memory by a coalesced warp load.  Two TMEM accumulators let the epilogue of
+// one unit overlap the MMAs of the next.
 //
 // Every mbarrier wait is bounded: on time-out the kernel records a code in the
 // plan's error word, stops issuing work, drains its copies and MMAs (bounded),
@@ -58,33 +57,36 @@ namespace {
 constexpr int R = 32;            // window rows = MMA N
 constexpr int KT = 16;           // condensed columns per tile = MMA K (16-bit inputs)
 constexpr int MB = 128;          // output columns per unit = MMA M
-constexpr int STAGES = 16;
-constexpr int IDX_TILES = 32;           // tile column indices staged per producer warp per refill
-constexpr int PANEL_BYTES = MB * KT * 2;  // 4096
-constexpr int VAL_BYTES = R * KT * 2;     // 1024
-constexpr int STAGE_BYTES = PANEL_BYTES + VAL_BYTES;
-constexpr int TMEM_COLS = 2 * R;          // two accumulators
-constexpr int PRODUCER_THREADS = 128;  // cp.async producer
+constexpr int TPS = 4;           // tiles per pipeline stage: one stage = K of 64
+constexpr int STAGES = 4;  // 16 tiles in flight per CTA, ~82 KB: two CTAs per SM
+constexpr int IDX_TILES = 32;    // tile column indices staged per refill (a multiple of TPS)
+constexpr int TILE_PANEL_BYTES = MB * KT * 2;          // 4 KB of B panel per tile
+constexpr int PANEL_BYTES = TPS * TILE_PANEL_BYTES;    // 16 KB per stage
+constexpr int HALF_BYTES = PANEL_BYTES / 2;            // one 64-column half: 8 k-groups of 1 KB atoms
+constexpr int VAL_BYTES = R * KT * 2;                  // 1 KB of values per tile
+constexpr int STAGE_BYTES = PANEL_BYTES + TPS * VAL_BYTES;
+constexpr int TMEM_COLS = 2 * R;  // two accumulators
+constexpr int NUM_THREADS = 192;
 constexpr int EPI_THREADS = 128;
 constexpr unsigned long long WAIT_CYCLES = 4ull << 30;  // ~2 s at 2 GHz: no legitimate wait comes close
-
-template <bool TMA> constexpr int num_threads() { return TMA ? 192 : 288; }
+static_assert(IDX_TILES % TPS == 0, "stages must not straddle index refills");
 
 struct TcParams {
-    const int4 *windows;     // {first row, first tile, tiles, rows}
-    const int32_t *order;    // windows by decreasing tile count
+    const int4 *windows;     // {first row, first tile, tiles, rows}, by decreasing tile count
     const int32_t *tile_cols;
     const uint16_t *tile_vals;
     const void *B;
     long long ldb;
-    float *C;
-    long long ldc;
+    void *C;                 // fp32, or 16-bit with the epilogue
+    long long ldc;           // elements of C's type
     int ncols;
     int n_units;
     int nfb;                 // column blocks of 128
     int *err;
     unsigned long long wait_cycles;  // bound of every mbarrier wait
     int stall_test;          // self-test: the producer issues no copies, so waits must time out
+    int has_ep;              // apply `ep` (row scale, bias, ReLU, 16-bit C)
+    EpiParams ep;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -129,22 +131,12 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, vola
     }
 }
 
-__device__ __forceinline__ void cp_async_16(uint32_t dst, const void *src, uint32_t src_size)
-{
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_size) : "memory");
-}
-
-__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar)
-{
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
-}
-
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
 {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
-// Box of the tensor map (64 columns x 16 rows) at (x, y) -> dst.
+// Box of the tensor map (64 columns x 16 or 64 rows) at (x, y) -> dst.
 __device__ __forceinline__ void tma_box(uint32_t dst, const void *tmap, int x, int y, uint32_t bar)
 {
     asm volatile(
@@ -181,11 +173,40 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
            ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
 }
 
-// The two tensor maps over the B block of a launch: box 64 x 1 (gather4) and
-// box 64 x 16 (consecutive rows), both 128-byte swizzled.
+// Stage k of a unit in load order, for a unit of nst stages that starts at
+// stage rot.  Each window starts at its own offset (window index mod nst), so
+// CTAs that run different windows at the same time read different B rows; when
+// every window starts at stage 0, all CTAs request the same lines together and
+// queue on the L2 slices holding them.  The order is fixed per plan, so results
+// are deterministic.
+__device__ __forceinline__ int stage_at(int k, int rot, int nst) { return k + rot < nst ? k + rot : k + rot - nst; }
+
+// Epilogue of one output column f of a window's rows [row0, row0 + rows):
+// scale, bias, ReLU, then fp32 / fp16 / bf16 stores (a warp writes 32
+// consecutive columns of a row).
+__device__ __noinline__ void epilogue_store(const TcParams &p, int row0, int rows, int f, const float (&v)[32])
+{
+    const EpiParams &ep = p.ep;
+    const float b = ep.bias ? __ldg(ep.bias + f) : 0.0f;
+    for (int r = 0; r < rows; ++r) {
+        float x = v[r] * (ep.row_scale ? __ldg(ep.row_scale + row0 + r) : 1.0f) + b;
+        if (ep.relu) x = fmaxf(x, 0.0f);
+        const long long o = (long long)(row0 + r) * p.ldc + f;
+        if (ep.out == 0)
+            __stcs(static_cast<float *>(p.C) + o, x);
+        else if (ep.out == 1)
+            static_cast<__half *>(p.C)[o] = __float2half_rn(x);
+        else
+            static_cast<__nv_bfloat16 *>(p.C)[o] = __float2bfloat16_rn(x);
+    }
+}
+
+// The tensor maps over the B block of a launch, all 128-byte swizzled: box
+// 64 x 1 (gather4), 64 x 16 and 64 x 64 (consecutive rows).
 struct BMaps {
     CUtensorMap gather;
-    CUtensorMap box;
+    CUtensorMap box16;
+    CUtensorMap box64;
 };
 
 template <bool BF16>
@@ -235,18 +256,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <bool BF16, bool TMA>
-__global__ void __launch_bounds__(num_threads<TMA>(), 1) tc_kernel(const TcParams p, const __grid_constant__ BMaps maps)
+template <bool BF16>
+__global__ void __launch_bounds__(NUM_THREADS, 1) tc_kernel(const TcParams p, const __grid_constant__ BMaps maps)
 {
     extern __shared__ uint8_t smem_raw[];
-    // 1024-byte aligned stage ring, then barriers.
+    // 1024-byte aligned stage ring, then the index buffer and the barriers.
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    int32_t *idxbuf = (int32_t *)(smem + STAGES * STAGE_BYTES);  // [4 warps][IDX_TILES][KT]
-    uint64_t *bars = (uint64_t *)(smem + STAGES * STAGE_BYTES + 4 * IDX_TILES * KT * 4);
-    uint64_t *full = bars;                 // [STAGES] producers -> MMA
-    uint64_t *empty = bars + STAGES;       // [STAGES] MMA -> producers
-    uint64_t *accf = bars + 2 * STAGES;    // [2] MMA -> epilogue
-    uint64_t *acce = bars + 2 * STAGES + 2;// [2] epilogue -> MMA
+    int32_t *idxbuf = (int32_t *)(smem + STAGES * STAGE_BYTES);  // [IDX_TILES][KT]
+    uint64_t *bars = (uint64_t *)(smem + STAGES * STAGE_BYTES + IDX_TILES * KT * 4);
+    uint64_t *full = bars;                  // [STAGES] producer -> MMA
+    uint64_t *empty = bars + STAGES;        // [STAGES] MMA -> producer
+    uint64_t *accf = bars + 2 * STAGES;     // [2] MMA -> epilogue
+    uint64_t *acce = bars + 2 * STAGES + 2; // [2] epilogue -> MMA
     uint64_t *drain = bars + 2 * STAGES + 4;
     uint32_t *tmem_holder = (uint32_t *)(bars + 2 * STAGES + 5);
     volatile int *abort_flag = (volatile int *)(tmem_holder + 1);
@@ -257,9 +278,7 @@ __global__ void __launch_bounds__(num_threads<TMA>(), 1) tc_kernel(const TcParam
 
     if (tid == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            // TMA: the producer's arrive.expect_tx (TMA completes the bytes);
-            // cp.async: one noinc arrive per producer thread.
-            mbar_init(smem_u32(&full[s]), TMA ? 1 : PRODUCER_THREADS);
+            mbar_init(smem_u32(&full[s]), 1);  // the producer's arrive.expect_tx; TMA completes the bytes
             mbar_init(smem_u32(&empty[s]), 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -281,58 +300,80 @@ __global__ void __launch_bounds__(num_threads<TMA>(), 1) tc_kernel(const TcParam
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
 
-    if (TMA && warp == 5) {
-        // ---------------------------- TMA producer -----------------------------
+    if (warp == 5) {
+        // ------------------------------ producer -------------------------------
         // The warp stages the B-row indices of up to IDX_TILES tiles in shared
-        // memory with one coalesced load; lane 0 then issues per tile 2 box
-        // loads (consecutive rows) or 8 gather4 loads, and one bulk copy of the
-        // value tile.  Abort decisions are warp-uniform.
-        uint32_t g = 0;
+        // memory with one coalesced load; lane 0 then fills one stage per TPS
+        // tiles: one 64 x 64 box per column half when the stage's 64 B rows are
+        // consecutive, else per tile a 64 x 16 box (16 consecutive rows) or four
+        // gather4 loads, plus one bulk copy of the stage's value tiles.  Abort
+        // decisions are warp-uniform.
+        uint32_t g = 0;  // stages issued by this CTA
         bool ok = true;
-        const void *tm_g = &maps.gather;
-        const void *tm_b = &maps.box;
+        const void *tm_g = &maps.gather, *tm_16 = &maps.box16, *tm_64 = &maps.box64;
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(tm_g) : "memory");
-            asm volatile("prefetch.tensormap [%0];" ::"l"(tm_b) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(tm_16) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(tm_64) : "memory");
         }
         for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
-            const int4 w = p.windows[p.order[u / p.nfb]];
+            const int win = u / p.nfb;
+            const int4 w = p.windows[win];
             const int n0 = (u % p.nfb) * MB;
-            for (int t0 = 0; ok && t0 < w.z; t0 += IDX_TILES) {
-                const int nt = min(IDX_TILES, w.z - t0);
-                __syncwarp();  // previous indices consumed
-                for (int q = lane; q < nt * KT; q += 32) idxbuf[q] = __ldg(p.tile_cols + ((long long)w.y + t0) * KT + q);
-                __syncwarp();  // indices visible to the warp
-                for (int t = 0; t < nt; ++t, ++g) {
-                    const int s = g % STAGES;
-                    ok = __all_sync(0xffffffffu, wait_bounded(smem_u32(&empty[s]), ((g / STAGES) & 1) ^ 1, abort_flag,
-                                                              p.err, 1, p.wait_cycles));
-                    if (!ok) break;
-                    if (lane == 0 && !p.stall_test) {
-                        const uint32_t fb = smem_u32(&full[s]);
-                        const uint32_t panel = smem_u32(smem + s * STAGE_BYTES);
-                        const int32_t *ix = idxbuf + t * KT;
-                        mbar_expect_tx(fb, STAGE_BYTES);
-                        if (ix[KT - 1] - ix[0] == KT - 1) {
-                            // Columns are distinct and ascending, so a span of 15
-                            // means 16 consecutive B rows: two 64 x 16 boxes.
-                            tma_box(panel, tm_b, n0, ix[0], fb);
-                            tma_box(panel + 2048, tm_b, n0 + 64, ix[0], fb);
-                        } else {
+            const int nst = (w.z + TPS - 1) / TPS;  // stages of this unit (w.z >= 1)
+            const int rot = win % nst;
+            int chunk = -1;  // IDX_TILES-tile chunk whose indices are staged
+            for (int k = 0; ok && k < nst; ++k, ++g) {
+                const int t = stage_at(k, rot, nst) * TPS;  // first tile of the stage
+                if (t / IDX_TILES != chunk) {
+                    chunk = t / IDX_TILES;
+                    const int t0 = chunk * IDX_TILES, nt = min(IDX_TILES, w.z - t0);
+                    __syncwarp();  // previous indices consumed
+                    for (int q = lane; q < nt * KT; q += 32)
+                        idxbuf[q] = __ldg(p.tile_cols + ((long long)w.y + t0) * KT + q);
+                    __syncwarp();  // indices visible to the warp
+                }
+                const int s = g % STAGES;
+                const int n = min(TPS, w.z - t);  // tiles in this stage
+                ok = __all_sync(0xffffffffu, wait_bounded(smem_u32(&empty[s]), ((g / STAGES) & 1) ^ 1, abort_flag,
+                                                          p.err, 1, p.wait_cycles));
+                if (!ok) break;
+                if (lane == 0 && !p.stall_test) {
+                    const uint32_t fb = smem_u32(&full[s]);
+                    const uint32_t panel = smem_u32(smem + s * STAGE_BYTES);
+                    const int32_t *ix = idxbuf + (t - chunk * IDX_TILES) * KT;
+                    mbar_expect_tx(fb, (uint32_t)n * (TILE_PANEL_BYTES + VAL_BYTES));
+                    // A window's columns ascend, distinct except the padding of
+                    // its last tile, which repeats the last column.  So m
+                    // indices whose span is m - 1 and whose last two differ
+                    // are m consecutive B rows.
+                    if (n == TPS && ix[TPS * KT - 1] - ix[0] == TPS * KT - 1 && ix[TPS * KT - 2] != ix[TPS * KT - 1]) {
+                        tma_box(panel, tm_64, n0, ix[0], fb);
+                        tma_box(panel + HALF_BYTES, tm_64, n0 + 64, ix[0], fb);
+                    } else {
+                        for (int j = 0; j < n; ++j) {
+                            const int32_t *jx = ix + j * KT;
+                            const uint32_t tp = panel + j * TILE_PANEL_BYTES / 2;
+                            if (jx[KT - 1] - jx[0] == KT - 1 && jx[KT - 2] != jx[KT - 1]) {
+                                tma_box(tp, tm_16, n0, jx[0], fb);
+                                tma_box(tp + HALF_BYTES, tm_16, n0 + 64, jx[0], fb);
+                            } else {
 #pragma unroll
-                            for (int c = 0; c < 2; ++c)
+                                for (int c = 0; c < 2; ++c)
 #pragma unroll
-                                for (int q = 0; q < 4; ++q)
-                                    tma_gather4(panel + c * 2048 + (q >> 1) * 1024 + (q & 1) * 512, tm_g, n0 + 64 * c,
-                                                ix[4 * q], ix[4 * q + 1], ix[4 * q + 2], ix[4 * q + 3], fb);
+                                    for (int q = 0; q < 4; ++q)
+                                        tma_gather4(tp + c * HALF_BYTES + (q >> 1) * 1024 + (q & 1) * 512, tm_g,
+                                                    n0 + 64 * c, jx[4 * q], jx[4 * q + 1], jx[4 * q + 2],
+                                                    jx[4 * q + 3], fb);
+                            }
                         }
-                        bulk_copy(panel + PANEL_BYTES, p.tile_vals + ((long long)w.y + t0 + t) * (R * KT), VAL_BYTES,
-                                  fb);
                     }
+                    bulk_copy(panel + PANEL_BYTES, p.tile_vals + ((long long)w.y + t) * (R * KT),
+                              (uint32_t)n * VAL_BYTES, fb);
                 }
             }
         }
-        // Drain: the copies of the last STAGES tiles must have landed before the
+        // Drain: the copies of the last STAGES stages must have landed before the
         // CTA may exit (already true unless the kernel is aborting).
         if (lane == 0 && !p.stall_test) {
             int no_abort = 0;
@@ -341,50 +382,6 @@ __global__ void __launch_bounds__(num_threads<TMA>(), 1) tc_kernel(const TcParam
                              p.wait_cycles);
         }
         __syncwarp();
-    } else if (!TMA && warp >= 5) {
-        // --------------------------- cp.async producers -------------------------
-        // Each producer warp stages the B-row indices of up to IDX_TILES tiles in
-        // its own shared-memory slice with one cooperative load, so no cp.async
-        // waits on a dependent load.  Only warp-level syncs are used, and every
-        // abort decision is warp-uniform, so a time-out cannot strand a barrier.
-        const int pt = tid - 160;       // 0..127
-        const int pw = pt >> 5;         // producer warp 0..3: column chunks 4pw..4pw+3
-        const int kr = lane & 7;        // row within a core matrix
-        const int cc = pw * 4 + (lane >> 3);
-        int32_t *widx = idxbuf + pw * IDX_TILES * KT;
-        const char *Bb = (const char *)p.B;
-        uint32_t g = 0;
-        bool ok = true;
-        for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
-            const int4 w = p.windows[p.order[u / p.nfb]];
-            const int f = (u % p.nfb) * MB + cc * 8;  // first of this thread's 8 columns
-            const bool fvalid = f < p.ncols;
-            for (int t0 = 0; ok && t0 < w.z; t0 += IDX_TILES) {
-                const int nt = min(IDX_TILES, w.z - t0);
-                __syncwarp();  // previous indices consumed
-                for (int q = lane; q < nt * KT; q += 32) widx[q] = __ldg(p.tile_cols + ((long long)w.y + t0) * KT + q);
-                __syncwarp();  // indices visible to the warp
-                for (int t = 0; t < nt; ++t, ++g) {
-                    const int s = g % STAGES;
-                    ok = __all_sync(0xffffffffu, wait_bounded(smem_u32(&empty[s]), ((g / STAGES) & 1) ^ 1, abort_flag,
-                                                              p.err, 1, p.wait_cycles));
-                    if (!ok) break;
-                    if (p.stall_test) continue;
-                    const long long tile = (long long)w.y + t0 + t;
-                    const uint32_t panel = smem_u32(smem + s * STAGE_BYTES);
-#pragma unroll
-                    for (int i = 0; i < 2; ++i) {
-                        const int brow = widx[t * KT + i * 8 + kr];
-                        const char *src = fvalid ? Bb + ((long long)brow * p.ldb + f) * 2 : Bb;
-                        cp_async_16(panel + cc * 256 + i * 128 + kr * 16, src, fvalid ? 16u : 0u);
-                    }
-                    if (pt < VAL_BYTES / 16)
-                        cp_async_16(panel + PANEL_BYTES + pt * 16, p.tile_vals + tile * (R * KT) + pt * 8, 16u);
-                    cp_async_arrive_noinc(smem_u32(&full[s]));
-                }
-            }
-        }
-        asm volatile("cp.async.wait_all;" ::: "memory");
     } else if (warp == 4) {
         // ------------------------------ MMA issuer -----------------------------
         if (lane == 0) {
@@ -392,24 +389,31 @@ __global__ void __launch_bounds__(num_threads<TMA>(), 1) tc_kernel(const TcParam
             uint32_t g = 0, i = 0;
             bool ok = true;
             for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x, ++i) {
-                const int4 w = p.windows[p.order[u / p.nfb]];
+                const int4 w = p.windows[u / p.nfb];
                 const uint32_t a = i & 1;
                 if (!wait_bounded(smem_u32(&acce[a]), ((i >> 1) & 1) ^ 1, abort_flag, p.err, 2, p.wait_cycles)) break;
                 tc_fence_after();
                 const uint32_t dcol = tmem + a * R;
-                for (int t = 0; t < w.z; ++t, ++g) {
+                // Stages in the producer's order: TPS tiles each, starting at
+                // the window's stage offset.
+                const int nst = (w.z + TPS - 1) / TPS;
+                const int rot = (u / p.nfb) % nst;
+                for (int k = 0; k < nst; ++k, ++g) {
                     const int s = g % STAGES;
+                    const int t = stage_at(k, rot, nst) * TPS;
+                    const int n = min(TPS, w.z - t);
                     if (!wait_bounded(smem_u32(&full[s]), (g / STAGES) & 1, abort_flag, p.err, 2, p.wait_cycles)) {
                         ok = false;
                         break;
                     }
-                    if (!TMA) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // cp.async wrote it
                     tc_fence_after();
                     const uint32_t panel = smem_u32(smem + s * STAGE_BYTES);
-                    const uint64_t adesc = TMA ? smem_desc(panel, 2048, 1024, 2)   // MN-major, 128-byte swizzle
-                                               : smem_desc(panel, 128, 256, 0);    // MN-major, no swizzle
-                    const uint64_t bdesc = smem_desc(panel + PANEL_BYTES, 128, 256, 0);  // K-major, no swizzle
-                    mma_f16(dcol, adesc, bdesc, idesc, t > 0 ? 1u : 0u);
+                    for (int j = 0; j < n; ++j) {
+                        // A: MN-major, 128-byte swizzle; B: K-major, no swizzle.
+                        const uint64_t adesc = smem_desc(panel + j * 2048, HALF_BYTES, 1024, 2);
+                        const uint64_t bdesc = smem_desc(panel + PANEL_BYTES + j * VAL_BYTES, 128, 256, 0);
+                        mma_f16(dcol, adesc, bdesc, idesc, (k | j) != 0 ? 1u : 0u);
+                    }
                     mma_commit(smem_u32(&empty[s]));
                 }
                 if (!ok) break;
@@ -425,7 +429,7 @@ __global__ void __launch_bounds__(num_threads<TMA>(), 1) tc_kernel(const TcParam
         // ------------------------------ epilogue -------------------------------
         uint32_t i = 0;
         for (int u = blockIdx.x; u < p.n_units; u += gridDim.x, ++i) {
-            const int4 w = p.windows[p.order[u / p.nfb]];
+            const int4 w = p.windows[u / p.nfb];
             const uint32_t a = i & 1;
             if (!__all_sync(0xffffffffu,
                             wait_bounded(smem_u32(&accf[a]), (i >> 1) & 1, abort_flag, p.err, 4, p.wait_cycles)))
@@ -437,10 +441,14 @@ __global__ void __launch_bounds__(num_threads<TMA>(), 1) tc_kernel(const TcParam
             mbar_arrive(smem_u32(&acce[a]));
             const int f = (u % p.nfb) * MB + warp * 32 + lane;
             if (f < p.ncols) {
-                float *c = p.C + (long long)w.x * p.ldc + f;
+                if (!p.has_ep) {
+                    float *c = static_cast<float *>(p.C) + (long long)w.x * p.ldc + f;
 #pragma unroll
-                for (int r = 0; r < R; ++r)
-                    if (r < w.w) __stcs(c + (long long)r * p.ldc, v[r]);
+                    for (int r = 0; r < R; ++r)
+                        if (r < w.w) __stcs(c + (long long)r * p.ldc, v[r]);
+                } else {
+                    epilogue_store(p, w.x, w.w, f, v);
+                }
             }
         }
     }
@@ -455,7 +463,7 @@ __global__ void __launch_bounds__(num_threads<TMA>(), 1) tc_kernel(const TcParam
 
 // Tail: 2 * STAGES + 5 mbarriers, the TMEM address and the abort flag.
 constexpr size_t kBarBytes = (2 * STAGES + 5) * 8 + 8;
-constexpr size_t kSmemBytes = 1024 + STAGES * STAGE_BYTES + 4 * IDX_TILES * KT * 4 + (kBarBytes + 127) / 128 * 128;  // ~89 KB
+constexpr size_t kSmemBytes = 1024 + STAGES * STAGE_BYTES + IDX_TILES * KT * 4 + (kBarBytes + 127) / 128 * 128;  // ~85 KB
 
 template <typename X>
 tcaspmm_status upload_vec(Shard *sh, X **dst, const std::vector<X> &v, const char *what)
@@ -494,7 +502,7 @@ EncodeTiledFn encode_fn()
 }
 
 // Tensor maps over a B block of ncols columns x K rows (x = column, zero fill
-// beyond ncols; y = B row), 128-byte swizzle, boxes 64 x 1 and 64 x 16.
+// beyond ncols; y = B row), 128-byte swizzle, boxes 64 x 1, 64 x 16, 64 x 64.
 tcaspmm_status encode_b_maps(tcaspmm_dtype dt, const void *dB, int64_t ncols, int64_t K, int64_t ldb, BMaps *m)
 {
     EncodeTiledFn fn = encode_fn();
@@ -503,30 +511,32 @@ tcaspmm_status encode_b_maps(tcaspmm_dtype dt, const void *dB, int64_t ncols, in
     const cuuint64_t strides[1] = {(cuuint64_t)ldb * 2};
     const cuuint32_t estr[2] = {1, 1};
     const CUtensorMapDataType ty = dt == TCASPMM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    const cuuint32_t box1[2] = {64, 1}, box16[2] = {64, 16};
-    CUresult r = fn(&m->gather, ty, 2, const_cast<void *>(dB), dims, strides, box1, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r == CUDA_SUCCESS)
-        r = fn(&m->box, ty, 2, const_cast<void *>(dB), dims, strides, box16, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+    // Boxes of 16 / 64 rows are used only where that many consecutive B rows
+    // exist, so on a B of fewer rows they are clipped to K (never issued).
+    const cuuint32_t k16 = (cuuint32_t)std::min<int64_t>(KT, K), k64 = (cuuint32_t)std::min<int64_t>(TPS * KT, K);
+    const cuuint32_t boxes[3][2] = {{64, 1}, {64, k16}, {64, k64}};
+    CUtensorMap *maps[3] = {&m->gather, &m->box16, &m->box64};
+    CUresult r = CUDA_SUCCESS;
+    for (int i = 0; i < 3 && r == CUDA_SUCCESS; ++i)
+        r = fn(maps[i], ty, 2, const_cast<void *>(dB), dims, strides, boxes[i], estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? TCASPMM_OK : fail(TCASPMM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
 }
 
 static_assert(sizeof(BMaps) <= sizeof(Shard::maps), "tensor-map storage in Shard");
 
-template <bool BF16, bool TMA>
+template <bool BF16>
 cudaError_t smem_optin()
 {
-    return cudaFuncSetAttribute(tc_kernel<BF16, TMA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    return cudaFuncSetAttribute(tc_kernel<BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
 }
 
-template <bool TMA>
 void launch_kernel(bool bf16, int grid, const TcParams &p, const BMaps &maps, cudaStream_t st)
 {
     if (bf16)
-        tc_kernel<true, TMA><<<grid, num_threads<TMA>(), kSmemBytes, st>>>(p, maps);
+        tc_kernel<true><<<grid, NUM_THREADS, kSmemBytes, st>>>(p, maps);
     else
-        tc_kernel<false, TMA><<<grid, num_threads<TMA>(), kSmemBytes, st>>>(p, maps);
+        tc_kernel<false><<<grid, NUM_THREADS, kSmemBytes, st>>>(p, maps);
 }
 
 }  // namespace
@@ -546,10 +556,9 @@ tcaspmm_status tc_upload(const tcaspmm_csr &, tcaspmm_dtype dt, Shard *sh)
     if (sh->n_windows == 0) return TCASPMM_OK;
     if (T.R != R || T.KT != KT) return fail(TCASPMM_ERR_UNSUPPORTED, "tile shape %dx%d not built", T.R, T.KT);
     // Windows by decreasing tile count, so the persistent grid balances.
-    std::vector<int32_t> order(sh->n_windows);
-    for (int i = 0; i < sh->n_windows; i++) order[i] = i;
-    std::stable_sort(order.begin(), order.end(),
-                     [&](int32_t a, int32_t b) { return T.windows[a].z > T.windows[b].z; });
+    // (Sorted on the host, so the kernel reads a unit's window with one load.)
+    std::vector<Int4> windows(T.windows);
+    std::stable_sort(windows.begin(), windows.end(), [](const Int4 &a, const Int4 &b) { return a.z > b.z; });
     // Value tiles -> shared-memory image (K-major, no swizzle, LBO 128 B, SBO 256 B).
     const size_t ntiles = T.tile_cols.size() / KT;
     std::vector<uint16_t> img(ntiles * R * KT);
@@ -565,35 +574,32 @@ tcaspmm_status tc_upload(const tcaspmm_csr &, tcaspmm_dtype dt, Shard *sh)
     std::vector<Int2> fb;
     for (const Int4 &w : T.windows) fb.push_back(Int2{w.x, w.x + w.w});
     tcaspmm_status s;
-    if ((s = upload_vec(sh, &sh->tc_windows, T.windows, "tc windows")) != TCASPMM_OK) return s;
-    if ((s = upload_vec(sh, &sh->tc_order, order, "tc order")) != TCASPMM_OK) return s;
+    if ((s = upload_vec(sh, &sh->tc_windows, windows, "tc windows")) != TCASPMM_OK) return s;
     if ((s = upload_vec(sh, &sh->tc_cols, T.tile_cols, "tc columns")) != TCASPMM_OK) return s;
     if ((s = upload_vec(sh, (uint16_t **)&sh->tc_vals, img, "tc values")) != TCASPMM_OK) return s;
     if ((s = upload_vec(sh, &sh->tc_fallback, fb, "tc fallback ranges")) != TCASPMM_OK) return s;
     int nsm = 148;
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, sh->device);
     sh->num_sms = nsm;
-    // Producer: TMA unless TCASPMM_TC_PRODUCER=cpasync.
-    const char *prod = std::getenv("TCASPMM_TC_PRODUCER");
-    sh->tc_tma = !(prod && std::strcmp(prod, "cpasync") == 0);
     // More than 48 KB of dynamic shared memory needs the opt-in, per device.
-    cudaError_t e = smem_optin<false, true>();
-    if (e == cudaSuccess) e = smem_optin<true, true>();
-    if (e == cudaSuccess) e = smem_optin<false, false>();
-    if (e == cudaSuccess) e = smem_optin<true, false>();
+    cudaError_t e = smem_optin<false>();
+    if (e == cudaSuccess) e = smem_optin<true>();
+    int per_sm = 0;
+    if (e == cudaSuccess)
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tc_kernel<false>, NUM_THREADS, kSmemBytes);
+    sh->tc_ctas_per_sm = std::max(1, per_sm);
     return e == cudaSuccess ? TCASPMM_OK : cuda_fail(e, "tc kernel shared-memory opt-in");
 }
 
-tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int64_t ldb, float *dC, int64_t ldc,
-                         cudaStream_t st)
+tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int64_t ldb, void *dC, int64_t ldc,
+                         const Epilogue *ep, cudaStream_t st)
 {
     if (sh.n_windows == 0 || sh.ncols == 0) return TCASPMM_OK;
     const bool aligned = ((uintptr_t)dB % 16 == 0) && ((ldb * 2) % 16 == 0) && (sh.ncols % 8 == 0);
     if (!aligned)  // CUDA-core fallback over the tc rows: whole rows, no segments
-        return launch_residue(sh, dt, dB, ldb, dC, ldc, st, sh.tc_fallback, sh.n_windows);
+        return launch_residue(sh, dt, dB, ldb, dC, ldc, ep, st, sh.tc_fallback, sh.n_windows);
     TcParams p;
     p.windows = (const int4 *)sh.tc_windows;
-    p.order = sh.tc_order;
     p.tile_cols = sh.tc_cols;
     p.tile_vals = (const uint16_t *)sh.tc_vals;
     p.B = dB;
@@ -606,21 +612,19 @@ tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int6
     p.err = sh.err;
     p.wait_cycles = WAIT_CYCLES;
     p.stall_test = 0;
-    const int grid = std::min(p.n_units, 4 * sh.num_sms);
-    if (sh.tc_tma) {
-        // Tensor maps depend on the B block: rebuilt only when it changes.
-        if (!(sh.maps_valid && sh.maps_ptr == dB && sh.maps_ldb == ldb)) {
-            sh.maps_valid = false;
-            tcaspmm_status ms = encode_b_maps(dt, dB, sh.ncols, sh.K, ldb, (BMaps *)sh.maps);
-            if (ms != TCASPMM_OK) return ms;
-            sh.maps_valid = true;
-            sh.maps_ptr = dB;
-            sh.maps_ldb = ldb;
-        }
-        launch_kernel<true>(dt == TCASPMM_BF16, grid, p, *(const BMaps *)sh.maps, st);
-    } else {
-        launch_kernel<false>(dt == TCASPMM_BF16, grid, p, BMaps{}, st);
+    p.has_ep = ep != nullptr;
+    p.ep = ep ? EpiParams{ep->row_scale, ep->bias, ep->relu, ep->out} : EpiParams{nullptr, nullptr, 0, 0};
+    const int grid = std::min(p.n_units, sh.tc_ctas_per_sm * sh.num_sms);  // persistent
+    // Tensor maps depend on the B block: rebuilt only when it changes.
+    if (!(sh.maps_valid && sh.maps_ptr == dB && sh.maps_ldb == ldb)) {
+        sh.maps_valid = false;
+        tcaspmm_status ms = encode_b_maps(dt, dB, sh.ncols, sh.K, ldb, (BMaps *)sh.maps);
+        if (ms != TCASPMM_OK) return ms;
+        sh.maps_valid = true;
+        sh.maps_ptr = dB;
+        sh.maps_ldb = ldb;
     }
+    launch_kernel(dt == TCASPMM_BF16, grid, p, *(const BMaps *)sh.maps, st);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TCASPMM_OK : cuda_fail(e, "tc kernel launch");
 }
@@ -641,36 +645,32 @@ extern "C" tcaspmm_status tcaspmm_selftest_tc_timeout(int device, unsigned long 
     if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
     if (!tc_supported()) return fail(TCASPMM_ERR_UNSUPPORTED, "device %d is not sm_100", device);
     const int4 win = make_int4(0, 0, 1, R);
-    const int32_t order = 0;
     const std::vector<int32_t> cols(KT, 0);
     const std::vector<uint16_t> vals(R * KT, 0);
-    void *d_win = nullptr, *d_order = nullptr, *d_cols = nullptr, *d_vals = nullptr, *d_b = nullptr, *d_c = nullptr;
+    void *d_win = nullptr, *d_cols = nullptr, *d_vals = nullptr, *d_b = nullptr, *d_c = nullptr;
     int *d_err = nullptr;
     tcaspmm_status st = TCASPMM_OK;
     auto alloc = [&](void **ptr, size_t n) {
         if (st == TCASPMM_OK && (e = cudaMalloc(ptr, n)) != cudaSuccess) st = cuda_fail(e, "self-test allocation");
     };
     alloc(&d_win, sizeof(win));
-    alloc(&d_order, sizeof(order));
     alloc(&d_cols, cols.size() * 4);
     alloc(&d_vals, vals.size() * 2);
-    alloc(&d_b, KT * MB * 2);
+    alloc(&d_b, TPS * KT * MB * 2);
     alloc(&d_c, R * MB * 4);
     alloc((void **)&d_err, sizeof(int));
     BMaps maps;
     if (st == TCASPMM_OK) {
         cudaMemcpy(d_win, &win, sizeof(win), cudaMemcpyHostToDevice);
-        cudaMemcpy(d_order, &order, sizeof(order), cudaMemcpyHostToDevice);
         cudaMemcpy(d_cols, cols.data(), cols.size() * 4, cudaMemcpyHostToDevice);
         cudaMemcpy(d_vals, vals.data(), vals.size() * 2, cudaMemcpyHostToDevice);
-        cudaMemset(d_b, 0, KT * MB * 2);
+        cudaMemset(d_b, 0, TPS * KT * MB * 2);
         cudaMemset(d_err, 0, sizeof(int));
-        st = encode_b_maps(TCASPMM_F16, d_b, MB, KT, MB, &maps);
+        st = encode_b_maps(TCASPMM_F16, d_b, MB, TPS * KT, MB, &maps);
     }
     if (st == TCASPMM_OK) {
         TcParams p;
         p.windows = (const int4 *)d_win;
-        p.order = (const int32_t *)d_order;
         p.tile_cols = (const int32_t *)d_cols;
         p.tile_vals = (const uint16_t *)d_vals;
         p.B = d_b;
@@ -683,9 +683,11 @@ extern "C" tcaspmm_status tcaspmm_selftest_tc_timeout(int device, unsigned long 
         p.err = d_err;
         p.wait_cycles = wait_cycles;
         p.stall_test = 1;
-        e = smem_optin<false, true>();
+        p.has_ep = 0;
+        p.ep = EpiParams{nullptr, nullptr, 0, 0};
+        e = smem_optin<false>();
         if (e == cudaSuccess) {
-            launch_kernel<true>(false, 1, p, maps, 0);
+            launch_kernel(false, 1, p, maps, 0);
             e = cudaGetLastError();
         }
         if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -699,7 +701,7 @@ extern "C" tcaspmm_status tcaspmm_selftest_tc_timeout(int device, unsigned long 
                      : fail(TCASPMM_OK, "no time-out recorded");
         }
     }
-    for (void *ptr : {d_win, d_order, d_cols, d_vals, d_b, d_c, (void *)d_err})
+    for (void *ptr : {d_win, d_cols, d_vals, d_b, d_c, (void *)d_err})
         if (ptr) cudaFree(ptr);
     return st;
 }

@@ -9,17 +9,22 @@ on X's current stream: a plan (host preprocessing + one upload of A) is built th
 first time a given (A, N, dtype, device) is seen and reused afterwards, so a GNN layer
 pays the preprocessing once per graph.  The gradient with respect to X is
 ``A^T @ dY``, computed with a second cached plan over the transpose of A; A's values
-are treated as constants (the graph does not train).  There is no CPU or PyTorch
-fallback: without the library or a CUDA device the op raises.
+are treated as constants (the graph does not train).
+
+    Y = torch.ops.tcaspmm.spmm_fused(crow, col, val, X, row_scale, bias, relu, out_dtype)
+
+applies the plan's fused epilogue (row scale, bias, ReLU, fp32/fp16/bf16 output) in
+the same kernels; its backward gives dX (through A^T) and d(bias).  There is no CPU or
+PyTorch fallback: without the library or a CUDA device the ops raise.
 """
 from __future__ import annotations
 
-from typing import Dict, Tuple
+from typing import Dict, Optional, Tuple
 
 import numpy as np
 import torch
 
-from . import CSR, Plan, as_dtype
+from . import CSR, Epilogue, Plan, as_dtype
 
 _PLANS: Dict[Tuple, Plan] = {}
 _MAX_PLANS = 16
@@ -112,14 +117,75 @@ def _backward(ctx, grad):
 spmm.register_autograd(_backward, setup_context=_setup)
 
 
-class GCNAggregate(torch.nn.Module):
-    """Y = A_hat @ X with a fixed normalised adjacency A_hat in CSR (the GCN propagation step)."""
+_OUT = {torch.float32: "f32", torch.float16: "f16", torch.bfloat16: "bf16"}
 
-    def __init__(self, crow: torch.Tensor, col: torch.Tensor, val: torch.Tensor):
+
+@torch.library.custom_op("tcaspmm::spmm_fused", mutates_args=())
+def spmm_fused(crow: torch.Tensor, col: torch.Tensor, val: torch.Tensor, X: torch.Tensor,
+               row_scale: Optional[torch.Tensor], bias: Optional[torch.Tensor], relu: bool,
+               out_dtype: torch.dtype) -> torch.Tensor:
+    """relu?(row_scale[:, None] * (A @ X) + bias) stored as out_dtype, in one pass (the
+    plan's fused epilogue: no separate elementwise kernels, 16-bit C halves C's bytes)."""
+    if not X.is_cuda:
+        raise ValueError("tcaspmm::spmm_fused needs X on a CUDA device")
+    if out_dtype not in _OUT:
+        raise ValueError(f"out_dtype must be float32, float16 or bfloat16, not {out_dtype}")
+    X = X.contiguous()
+    M = crow.shape[0] - 1
+    p = _plan(crow, col, val, X.shape[0], X, transposed=False)
+    out = torch.empty((M, X.shape[1]), device=X.device, dtype=out_dtype)
+    rs = row_scale.to(X.device, torch.float32).contiguous() if row_scale is not None else None
+    b = bias.to(X.device, torch.float32).contiguous() if bias is not None else None
+    p.execute1(X, out, torch.cuda.current_stream(X.device), epilogue=Epilogue(rs, b, relu, _OUT[out_dtype]))
+    return out
+
+
+@spmm_fused.register_fake
+def _(crow, col, val, X, row_scale, bias, relu, out_dtype):
+    return X.new_empty((crow.shape[0] - 1, X.shape[1]), dtype=out_dtype)
+
+
+def _setup_fused(ctx, inputs, output):
+    crow, col, val, X, row_scale, bias, relu, out_dtype = inputs
+    ctx.save_for_backward(crow, col, val, row_scale, output if relu else None)
+    ctx.ncol = X.shape[0]
+    ctx.x_dtype = X.dtype
+    ctx.has_bias = bias is not None
+
+
+def _backward_fused(ctx, grad):
+    # Y = relu(s * (A X) + b):  dZ = dY * [Y > 0],  dX = A^T (s * dZ),  db = sum_r dZ.
+    crow, col, val, row_scale, Y = ctx.saved_tensors
+    dZ = grad.float()
+    if Y is not None:
+        dZ = dZ * (Y > 0)
+    db = dZ.sum(0) if ctx.has_bias else None
+    if row_scale is not None:
+        dZ = dZ * row_scale.to(dZ.device, torch.float32)[:, None]
+    dX = torch.ops.tcaspmm.spmm_t(crow, col, val, dZ.to(ctx.x_dtype), ctx.ncol)
+    return None, None, None, dX.to(ctx.x_dtype), None, db, None, None
+
+
+spmm_fused.register_autograd(_backward_fused, setup_context=_setup_fused)
+
+
+class GCNAggregate(torch.nn.Module):
+    """Y = relu?(row_scale * (A_hat @ X) + bias) with a fixed adjacency A_hat in CSR (the GCN /
+    GraphSAGE-mean propagation step); without row_scale, bias or relu it is plain A_hat @ X."""
+
+    def __init__(self, crow: torch.Tensor, col: torch.Tensor, val: torch.Tensor,
+                 row_scale: Optional[torch.Tensor] = None, bias: Optional[torch.Tensor] = None,
+                 relu: bool = False):
         super().__init__()
         self.register_buffer("crow", crow)
         self.register_buffer("col", col)
         self.register_buffer("val", val)
+        self.register_buffer("row_scale", row_scale)
+        self.bias = bias
+        self.relu = relu
 
     def forward(self, X: torch.Tensor) -> torch.Tensor:
-        return torch.ops.tcaspmm.spmm(self.crow, self.col, self.val, X)
+        if self.row_scale is None and self.bias is None and not self.relu:
+            return torch.ops.tcaspmm.spmm(self.crow, self.col, self.val, X)
+        return torch.ops.tcaspmm.spmm_fused(self.crow, self.col, self.val, X, self.row_scale, self.bias,
+                                            self.relu, torch.float32)

@@ -225,6 +225,42 @@ def test_tensor_core_integer_values_bit_exact():
     np.testing.assert_array_equal(out, reference(A, B, "f16").astype(np.float32))
 
 
+@pytest.mark.parametrize("dt", ["f32", "f16"])
+def test_row_split_plan_on_one_device(dt):
+    """Row-split plan with two shards placed on cuda:0: each shard writes its row
+    block of C from the whole B; tensor-core windows and residue rows in both."""
+    A = _vstack(T.gen_uniform(256, 4096, 0.3, 1), T.gen_rmat(12, 60000, kind="gcn", seed=9))
+    A = _vstack(A, T.gen_uniform(96, 4096, 0.3, 2))
+    N = 64
+    B = T.gen_dense(A.ncol, N, 4, "f32")
+    Bd = torch.from_numpy(B).to(_torch_dt(dt)).cuda()
+    Cd = torch.full((A.nrow, N), float("nan"), device="cuda")
+    scale = torch.rand(A.nrow, device="cuda") + 0.5
+    Ce = torch.full((A.nrow, N), float("nan"), device="cuda")
+    with T.Plan(A, N, dt, num_gpus=2, devices=[0, 0], split="rows") as p:
+        blocks = [p.shard_rows(s) for s in range(2)]
+        assert blocks[0][0] == 0 and blocks[0][1] + blocks[1][1] == A.nrow and blocks[1][1] > 0
+        p.execute([Bd, Bd], [Cd[r0:r0 + rc] for r0, rc in blocks])
+        p.execute([Bd, Bd], [Ce[r0:r0 + rc] for r0, rc in blocks],
+                  epilogues=[T.Epilogue(row_scale=scale[r0:r0 + rc]) for r0, rc in blocks])
+        p.sync_check()
+        st = p.stats
+    if dt == "f16":
+        assert st["tc_windows"] >= 10 and st["residue_nnz"] > 0
+    ref = reference(A, B, dt)
+    tol = TOL_TC if st["tc_nnz"] else TOL_CORE
+    assert oracle.rel_l2(Cd.cpu().numpy(), ref) <= tol
+    assert oracle.rel_l2(Ce.cpu().numpy(), ref * scale.cpu().numpy()[:, None]) <= tol
+    # One plan per rank (the torchrun form) gives the same blocks.
+    for r, (r0, rc) in enumerate(blocks):
+        Cr = torch.empty((rc, N), device="cuda")
+        with T.Plan(A, N, dt, rank=r, world=2, device=0, split="rows") as q:
+            assert q.shard_rows(0) == (r0, rc)
+            q.execute1(Bd, Cr)
+            q.sync_check()
+        torch.testing.assert_close(Cr, Cd[r0:r0 + rc], rtol=0, atol=0)
+
+
 def test_tensor_core_wait_time_out_is_reported_and_recoverable():
     """A wait that nothing will satisfy ends in TCASPMM_ERR_TIMEOUT, not a hang, and the GPU stays usable."""
     import ctypes
@@ -237,3 +273,39 @@ def test_tensor_core_wait_time_out_is_reported_and_recoverable():
     assert status == T.Status.TIMEOUT, T.last_error()
     assert code.value & 2  # the MMA thread's wait on the producer ran out
     check(T.gen_uniform(256, 256, 0.4, 14), 128, "f16")  # the context still works
+
+
+def _window_union_matrix(unions, K, seed=21, drop=0.1):
+    """One 32-row window per column union; each row keeps ~90% of its window's columns, small integer values."""
+    rng = np.random.default_rng(seed)
+    rp, cols, vals = [0], [], []
+    for u in unions:
+        u = np.asarray(u, np.int32)
+        for r in range(32):
+            keep = u[rng.random(u.size) >= drop] if r else u  # row 0 carries the whole union
+            cols.append(keep)
+            vals.append(rng.integers(-3, 4, keep.size).astype(np.float32))
+            rp.append(rp[-1] + keep.size)
+    return T.CSR(32 * len(unions), K, np.asarray(rp, np.int64), np.concatenate(cols), np.concatenate(vals))
+
+
+def test_tensor_core_stage_shapes_bit_exact():
+    """Every producer form: 64-row boxes, 16-row boxes, gather4 tiles, partial stages,
+    index refills past 32 tiles, and a padded last tile whose span looks like 16
+    consecutive rows ({.., 40, 55, 55, ..}) but is not."""
+    K = 2048
+    unions = [
+        list(range(32)) + [40, 55],                                   # padded tile of span 15
+        list(range(64)) + [70, 71, 72, 73] + list(range(100, 116)),   # one 64-row stage, then gather + padded
+        [c for c in range(65) if c != 30],                            # span 64 over 64 columns: per-tile forms
+        list(range(0, K, 2)),                                         # 64 gathered tiles, two index refills
+        list(range(1024)),                                            # 16 stages of 64 consecutive rows
+        list(range(1000, 1016)) + list(range(1017, 1033)),            # 16-row box, then a 16-span gap tile
+    ]
+    A = _window_union_matrix(unions, K)
+    B = np.round(T.gen_dense(K, 256, 5, "f32") * 4).astype(np.float32)
+    for dt in ("f16", "bf16"):
+        for N in (256, 136):
+            out, st = run(A, B[:, :N], dt)
+            assert st["tc_windows"] == len(unions) and st["tc_nnz"] == st["nnz"], st
+            np.testing.assert_array_equal(out, reference(A, B[:, :N], dt).astype(np.float32))

@@ -160,6 +160,28 @@ def test_partition_columns_tile_n_disjointly(N, dt, world):
     assert np.all(covered == 1)
 
 
+@pytest.mark.parametrize("parts", [1, 2, 3, 8, 5000])
+def test_partition_rows_covers_rows_in_balanced_blocks(parts):
+    A = T.gen_rmat(12, 40000, kind="gcn", seed=3)
+    rb = T.partition_rows(A, parts)
+    assert rb[0] == 0 and rb[-1] == A.nrow and np.all(np.diff(rb) >= 0)
+    cost = np.diff(A.row_ptr[rb] + 2 * rb)
+    row_cost = np.diff(A.row_ptr) + 2
+    # Each block is within one row's cost of the ideal share.
+    assert np.all(np.abs(cost - cost.sum() / parts) <= row_cost.max() + 1)
+    assert np.array_equal(T.partition_rows(A, parts), rb)  # deterministic
+
+
+def test_partition_rows_edge_cases():
+    empty = T.CSR(0, 5, np.zeros(1, np.int64), np.zeros(0, np.int32), np.zeros(0, np.float32))
+    assert list(T.partition_rows(empty, 3)) == [0, 0, 0, 0]
+    one = T.CSR(1, 4, np.array([0, 2], np.int64), np.array([0, 3], np.int32), np.ones(2, np.float32))
+    rb = T.partition_rows(one, 4)
+    assert rb[0] == 0 and rb[-1] == 1 and np.all(np.diff(rb) >= 0)
+    with pytest.raises(T.TcaspmmError):
+        T.partition_rows(one, 0)
+
+
 @pytest.mark.parametrize("case", ["c1_f16", "c1_f32", "sweep_mag", "skew", "gcn", "bundled", "empty_rows", "tiny"])
 def test_schedule_covers_every_nonzero_exactly_once(case, bundled):
     if case == "c1_f16":

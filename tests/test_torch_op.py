@@ -55,3 +55,45 @@ def test_gcn_layer_reuses_its_plan():
     y2 = layer(X)
     assert len(torch_op._PLANS) == 1
     torch.testing.assert_close(y1, y2, rtol=0, atol=0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_fused_op_forward_and_backward(out_dtype):
+    """relu(s * (A X) + b): forward and dX, db against dense fp64 torch on the CPU."""
+    A, crow, col, val = _graph(seed=4)
+    g = torch.Generator().manual_seed(2)
+    X = torch.randn(A.ncol, 48, generator=g).cuda().requires_grad_(True)
+    s = torch.rand(A.nrow, generator=g) + 0.5
+    b = torch.randn(48, generator=g).cuda().requires_grad_(True)
+    Y = torch.ops.tcaspmm.spmm_fused(crow, col, val, X, s.cuda(), b, True, out_dtype)
+    assert Y.dtype == out_dtype
+    Ad = torch.from_numpy(A.to_scipy().toarray()).double()
+    Xr = X.detach().cpu().double().requires_grad_(True)
+    br = b.detach().cpu().double().requires_grad_(True)
+    Yr = torch.relu(s.double()[:, None] * (Ad @ Xr) + br)
+    tol = 1e-5 if out_dtype == torch.float32 else 2.0 ** -8
+    assert oracle.rel_l2(Y.detach().float().cpu().numpy(), Yr.detach().numpy()) <= tol
+    G = torch.randn(Y.shape, generator=g)
+    (Y.float() * G.cuda()).sum().backward()
+    (Yr * G.double()).sum().backward()
+    # The ReLU mask comes from the rounded Y, so a bf16 output may flip entries at 0.
+    gtol = 1e-5 if out_dtype == torch.float32 else 2e-2
+    assert oracle.rel_l2(X.grad.cpu().numpy(), Xr.grad.numpy()) <= gtol
+    assert oracle.rel_l2(b.grad.cpu().numpy(), br.grad.numpy()) <= gtol
+
+
+@pytest.mark.gpu
+def test_sage_mean_layer_with_bias():
+    A, crow, col, val = _graph(seed=6)
+    deg = torch.from_numpy(np.diff(A.row_ptr)).float()
+    inv = torch.where(deg > 0, 1.0 / deg.clamp(min=1), torch.zeros_like(deg))
+    ones = torch.ones_like(val)
+    bias = torch.nn.Parameter(torch.zeros(32, device="cuda"))
+    layer = torch_op.GCNAggregate(crow, col, ones, row_scale=inv, bias=bias, relu=False)
+    X = torch.randn(A.ncol, 32, device="cuda")
+    Y = layer(X)
+    mean = oracle.spmm_f64(A.row_ptr, A.col, np.repeat(inv.numpy(), np.diff(A.row_ptr)), X.cpu().numpy())
+    assert oracle.rel_l2(Y.detach().cpu().numpy(), mean) <= 1e-5
+    Y.sum().backward()
+    assert bias.grad is not None and torch.allclose(bias.grad, torch.full_like(bias, A.nrow))
