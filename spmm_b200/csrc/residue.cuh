@@ -153,16 +153,37 @@ __device__ __forceinline__ void add_l2(const float *c, float (&a)[VEC])
     }
 }
 
+// Epilogue operands held in registers by a lane while it streams rows: the
+// bias of its VEC columns (loaded once per pass) and the scale of the current
+// row (loaded when the row starts, so the store at the row's end does not wait
+// on a load).  Empty without the epilogue.
+template <int VEC, bool EPI> struct EpiRegs {
+    __device__ __forceinline__ void load_bias(const ResidueParams &, int) {}
+    __device__ __forceinline__ void load_scale(const ResidueParams &, long long) {}
+};
+template <int VEC> struct EpiRegs<VEC, true> {
+    float bias[VEC];
+    float scale;
+    __device__ __forceinline__ void load_bias(const ResidueParams &p, int c0)
+    {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) bias[k] = p.ep.bias ? __ldg(p.ep.bias + c0 + k) : 0.0f;
+    }
+    __device__ __forceinline__ void load_scale(const ResidueParams &p, long long r)
+    {
+        scale = p.ep.row_scale ? __ldg(p.ep.row_scale + r) : 1.0f;
+    }
+};
+
 // Epilogue then store of VEC outputs of row r at column c0 of the block.
 template <int VEC>
-__device__ __forceinline__ void store_epi(const ResidueParams &p, long long r, int c0, float (&a)[VEC])
+__device__ __forceinline__ void store_epi(const ResidueParams &p, long long r, int c0, float (&a)[VEC],
+                                          const EpiRegs<VEC, true> &er)
 {
     const EpiParams &ep = p.ep;
-    const float s = ep.row_scale ? __ldg(ep.row_scale + r) : 1.0f;
 #pragma unroll
     for (int k = 0; k < VEC; ++k) {
-        float x = a[k] * s;
-        if (ep.bias) x += __ldg(ep.bias + c0 + k);
+        const float x = fmaf(a[k], er.scale, er.bias[k]);
         a[k] = ep.relu ? fmaxf(x, 0.0f) : x;
     }
     if (ep.out == 0) {
@@ -170,11 +191,11 @@ __device__ __forceinline__ void store_epi(const ResidueParams &p, long long r, i
         return;
     }
     // 16-bit outputs: VEC = 1 one element, 4 -> 8 bytes, 8 -> 16 bytes.
-    uint32_t h[(VEC + 1) / 2];
+    uint16_t *c = reinterpret_cast<uint16_t *>(p.C) + r * p.ldc + c0;
     if constexpr (VEC == 1) {
-        uint16_t *c = reinterpret_cast<uint16_t *>(p.C) + r * p.ldc + c0;
         *c = ep.out == 1 ? __half_as_ushort(__float2half_rn(a[0])) : __bfloat16_as_ushort(__float2bfloat16_rn(a[0]));
     } else {
+        uint32_t h[VEC / 2];
 #pragma unroll
         for (int k = 0; k < VEC / 2; ++k) {
             if (ep.out == 1) {
@@ -185,7 +206,6 @@ __device__ __forceinline__ void store_epi(const ResidueParams &p, long long r, i
                 h[k] = *reinterpret_cast<const uint32_t *>(&v);
             }
         }
-        uint16_t *c = reinterpret_cast<uint16_t *>(p.C) + r * p.ldc + c0;
         if constexpr (VEC == 4)
             __stcs(reinterpret_cast<uint2 *>(c), make_uint2(h[0], h[1]));
         else
@@ -195,10 +215,11 @@ __device__ __forceinline__ void store_epi(const ResidueParams &p, long long r, i
 
 // The store of a finished output slice: plain fp32, or through the epilogue.
 template <int VEC, bool EPI>
-__device__ __forceinline__ void emit(const ResidueParams &p, long long r, int c0, float (&a)[VEC])
+__device__ __forceinline__ void emit(const ResidueParams &p, long long r, int c0, float (&a)[VEC],
+                                     const EpiRegs<VEC, EPI> &er)
 {
     if constexpr (EPI)
-        store_epi<VEC>(p, r, c0, a);
+        store_epi<VEC>(p, r, c0, a, er);
     else
         store_c<VEC>(p.C + r * p.ldc + c0, a);
 }
@@ -247,16 +268,20 @@ __device__ __forceinline__ void stream_lean(const ResidueParams &p, int r_lo, in
     int e = __ldg(p.row_ptr + r + 1);
     int j = __ldg(p.row_ptr + r_lo);
     const int jend = __ldg(p.row_ptr + r_hi);
+    EpiRegs<VEC, EPI> er;
+    er.load_bias(p, c0);
+    er.load_scale(p, r);
     float acc[VEC];
 #pragma unroll
     for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
     auto pass_row_ends = [&](int jj) {
         while (jj >= e) {
-            emit<VEC, EPI>(p, r, c0, acc);
+            emit<VEC, EPI>(p, r, c0, acc, er);
 #pragma unroll
             for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
-            ++r;
+            ++r;  // < r_hi: nonzero jj < jend lies in a later row
             e = __ldg(p.row_ptr + r + 1);
+            er.load_scale(p, r);
         }
     };
     for (; j + U <= jend; j += U) {
@@ -283,10 +308,11 @@ __device__ __forceinline__ void stream_lean(const ResidueParams &p, int r_lo, in
         pass_row_ends(j);
         fma_raw<T, VEC>(v, rb, acc);
     }
-    for (; r < r_hi; ++r) {
-        emit<VEC, EPI>(p, r, c0, acc);
+    while (r < r_hi) {
+        emit<VEC, EPI>(p, r, c0, acc, er);
 #pragma unroll
         for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
+        if (++r < r_hi) er.load_scale(p, r);
     }
 }
 
@@ -358,7 +384,12 @@ __global__ void __launch_bounds__(256, EPI ? 3 : 4) residue_kernel(const Residue
                 for (int off = G; off < 32; off <<= 1)
 #pragma unroll
                     for (int k = 0; k < VEC; ++k) acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], off);
-                if (sub == 0 && c0 < p.ncols) emit<VEC, EPI>(p, L.x, c0, acc);
+                if (sub == 0 && c0 < p.ncols) {
+                    EpiRegs<VEC, EPI> er;
+                    er.load_bias(p, c0);
+                    er.load_scale(p, L.x);
+                    emit<VEC, EPI>(p, L.x, c0, acc, er);
+                }
             }
             if (lane == 0) p.counters[s.w] = 0u;  // ready for the next launch
         }

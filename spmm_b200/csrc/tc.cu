@@ -181,23 +181,26 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
 // are deterministic.
 __device__ __forceinline__ int stage_at(int k, int rot, int nst) { return k + rot < nst ? k + rot : k + rot - nst; }
 
-// Epilogue of one output column f of a window's rows [row0, row0 + rows):
-// scale, bias, ReLU, then fp32 / fp16 / bf16 stores (a warp writes 32
-// consecutive columns of a row).
-__device__ __noinline__ void epilogue_store(const TcParams &p, int row0, int rows, int f, const float (&v)[32])
+// Epilogue of one output column f of a window's rows [row0, row0 + rows), after
+// the row scales were applied: bias, ReLU, then fp32 / fp16 / bf16 stores (a
+// warp writes 32 consecutive columns of a row).
+__device__ __forceinline__ void epilogue_store(const TcParams &p, int row0, int rows, int f, const float (&v)[32])
 {
     const EpiParams &ep = p.ep;
     const float b = ep.bias ? __ldg(ep.bias + f) : 0.0f;
-    for (int r = 0; r < rows; ++r) {
-        float x = v[r] * (ep.row_scale ? __ldg(ep.row_scale + row0 + r) : 1.0f) + b;
-        if (ep.relu) x = fmaxf(x, 0.0f);
-        const long long o = (long long)(row0 + r) * p.ldc + f;
-        if (ep.out == 0)
-            __stcs(static_cast<float *>(p.C) + o, x);
-        else if (ep.out == 1)
-            static_cast<__half *>(p.C)[o] = __float2half_rn(x);
-        else
-            static_cast<__nv_bfloat16 *>(p.C)[o] = __float2bfloat16_rn(x);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        if (r < rows) {
+            float x = v[r] + b;
+            if (ep.relu) x = fmaxf(x, 0.0f);
+            const long long o = (long long)(row0 + r) * p.ldc + f;
+            if (ep.out == 0)
+                __stcs(static_cast<float *>(p.C) + o, x);
+            else if (ep.out == 1)
+                static_cast<__half *>(p.C)[o] = __float2half_rn(x);
+            else
+                static_cast<__nv_bfloat16 *>(p.C)[o] = __float2bfloat16_rn(x);
+        }
     }
 }
 
@@ -439,6 +442,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_kernel(const TcParams p, co
             tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + a * R, v);
             tc_fence_before();
             mbar_arrive(smem_u32(&acce[a]));
+            if (p.has_ep && p.ep.row_scale) {
+                // One coalesced load of the window's row scales, then a broadcast
+                // per row (all lanes converged here).
+                const float sc = lane < w.w ? __ldg(p.ep.row_scale + w.x + lane) : 1.0f;
+#pragma unroll
+                for (int r = 0; r < R; ++r) v[r] *= __shfl_sync(0xffffffffu, sc, r);
+            }
             const int f = (u % p.nfb) * MB + warp * 32 + lane;
             if (f < p.ncols) {
                 if (!p.has_ep) {
