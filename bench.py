@@ -341,6 +341,17 @@ def main():
         cs_err = float((Cs - Cd).norm() / max(Cd.norm(), 1e-30)) if ep is None else None
     except Exception as e:  # reported
         ms_cusparse, cs_err = None, str(e)
+    # Blocked-ELL (32 x 32 blocks) where A is small enough to be dense-ish (C1 / C2 shapes).
+    bell = None
+    if dt != "f32" and M * K <= 1 << 26 and args.split == "columns" and ep is None:
+        try:
+            Cb = torch.empty_like(Cd, dtype=torch.float32)
+            bell_ms, _ = T.cusparse_blocked_ell(A, 32, Bd, Cb, dt, warmup=3, iters=max(5, min(args.steps, 50)),
+                                                stream=stream) if world == 1 else (None, None)
+            bell = {"ms": bell_ms, "block": 32,
+                    "rel_diff": float((Cb - Cd).norm() / max(Cd.norm(), 1e-30)) if bell_ms else None}
+        except Exception as e:  # reported
+            bell = {"error": str(e)}
     gemm = None
     if M * K * elem <= 2**31 and args.split == "columns" and ep is None:
         Ad = torch.zeros((M, K), dtype=tdt, device=dev)
@@ -389,7 +400,7 @@ def main():
             "e2e": {"value": round(flops / (ms_e2e * 1e-3) / 1e9, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 4)},
             "baselines": {"spmm_cusparse_ms": ms_cusparse, "spmm_cusparse_rel_diff": cs_err,
-                          "gemm_cublas_ms": gemm,
+                          "gemm_cublas_ms": gemm, "spmm_cusparse_blocked_ell": bell,
                           "spmm_cusparse_gflops": round(flops / (ms_cusparse * 1e-3) / 1e9, 3)
                           if isinstance(ms_cusparse, float) else None},
             "cpu_baseline": cpu,

@@ -27,6 +27,17 @@ tcaspmm_status tcaspmm_cusparse_spmm(const int32_t *d_row_ptr, const int32_t *d_
 tcaspmm_status tcaspmm_cublas_gemm(const void *dA, const void *dB, float *dC, int64_t M, int64_t N, int64_t K,
                                    tcaspmm_dtype dt, int warmup, int iters, void *stream, double *ms_per_iter);
 
+/* cusparseSpMM with A in Blocked-ELL: the host CSR A is converted to blocks of
+ * block x block (every block-row padded to the widest one with column -1),
+ * values rounded to dt (16-bit only), then uploaded; B (K x N, ld ldb) and C (M
+ * x N fp32, ld ldc) as above, fp32 compute.  Replaces perform_cuSPARSE_BlockSpMM
+ * (src/spmm_cusparse.cu:181-444), which builds the same format from a dense A.
+ * M and K need not be multiples of block: A is padded with zero rows/columns and
+ * C gets only its M rows.  *ell_bytes = bytes of the Blocked-ELL arrays. */
+tcaspmm_status tcaspmm_cusparse_blocked_ell(const tcaspmm_csr *A, int block, const void *dB, int64_t ldb, float *dC,
+                                           int64_t ldc, int64_t N, tcaspmm_dtype dt, int warmup, int iters,
+                                           void *stream, double *ms_per_iter, int64_t *ell_bytes);
+
 /* Device CSR arrays that a plan uploaded for `shard` (int32 offsets, int32
  * columns, values in the plan's dtype); lets a baseline run on the same bytes. */
 tcaspmm_status tcaspmm_plan_device_csr(const tcaspmm_plan *plan, int shard, const int32_t **row_ptr,

@@ -513,7 +513,20 @@ def baselines():
         _blib.tcaspmm_cublas_gemm.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64, C.c_int, C.c_int, C.c_int, _vp,
                                               _P(C.c_double)]
         _blib.tcaspmm_cublas_gemm.restype = C.c_int
+        _blib.tcaspmm_cusparse_blocked_ell.argtypes = [_P(_CSR), C.c_int, _vp, _i64, _vp, _i64, _i64, C.c_int,
+                                                       C.c_int, C.c_int, _vp, _P(C.c_double), _P(_i64)]
+        _blib.tcaspmm_cusparse_blocked_ell.restype = C.c_int
     return _blib
+
+
+def cusparse_blocked_ell(A: CSR, block: int, B, Cout, dt, warmup: int = 5, iters: int = 10, stream=None):
+    """Time cusparseSpMM on A converted to Blocked-ELL (block x block); returns (ms per call, ELL bytes)."""
+    ms, nbytes = C.c_double(), _i64()
+    cA = A._c()
+    _check(baselines().tcaspmm_cusparse_blocked_ell(C.byref(cA), block, _ptr(B), int(B.stride(0)), _ptr(Cout),
+                                                    int(Cout.stride(0)), int(B.shape[1]), int(as_dtype(dt)), warmup,
+                                                    iters, _stream_handle(stream), C.byref(ms), C.byref(nbytes)))
+    return ms.value, nbytes.value
 
 
 def cusparse_spmm(plan: Plan, B, Cout, warmup: int = 10, iters: int = 10, stream=None, shard: int = 0) -> float:

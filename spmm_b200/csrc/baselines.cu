@@ -1,10 +1,16 @@
 // cuSPARSE and cuBLAS baselines (libtcaspmm_baselines.so).  Reported next to
 // tcaspmm, never called by it.
+#include <algorithm>
 #include <cstdio>
+#include <cstring>
+#include <vector>
 
 #include <cublas_v2.h>
 #include <cuda_runtime.h>
 #include <cusparse.h>
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "tcaspmm_baselines.h"
 
@@ -111,5 +117,113 @@ extern "C" tcaspmm_status tcaspmm_cublas_gemm(const void *dA, const void *dB, fl
     };
     tcaspmm_status s = time_loop(run, warmup, iters, st, ms_per_iter);
     cublasDestroy(h);
+    return s;
+}
+
+extern "C" tcaspmm_status tcaspmm_cusparse_blocked_ell(const tcaspmm_csr *A, int block, const void *dB, int64_t ldb,
+                                                      float *dC, int64_t ldc, int64_t N, tcaspmm_dtype dt, int warmup,
+                                                      int iters, void *stream, double *ms_per_iter, int64_t *ell_bytes)
+{
+    if (!A || !ms_per_iter || block < 1 || dt == TCASPMM_F32) return TCASPMM_ERR_INVALID_ARG;
+    tcaspmm_status s = tcaspmm_csr_validate(A);
+    if (s != TCASPMM_OK) return s;
+    const int64_t M = A->nrow, K = A->ncol;
+    const int64_t brows = (M + block - 1) / block, Mp = brows * block, Kp = (K + block - 1) / block * block;
+    // Nonzero block-columns of every block-row, ascending.
+    std::vector<std::vector<int32_t>> bcols((size_t)brows);
+    int64_t width = 0;
+    for (int64_t br = 0; br < brows; br++) {
+        std::vector<int32_t> &v = bcols[br];
+        for (int64_t r = br * block; r < std::min(M, (br + 1) * block); r++)
+            for (int64_t j = A->row_ptr[r]; j < A->row_ptr[r + 1]; j++) v.push_back(A->col_idx[j] / block);
+        std::sort(v.begin(), v.end());
+        v.erase(std::unique(v.begin(), v.end()), v.end());
+        width = std::max<int64_t>(width, (int64_t)v.size());
+    }
+    width = std::max<int64_t>(width, 1);
+    const int64_t ell_cols = width * block;
+    std::vector<int32_t> colidx((size_t)(brows * width), -1);
+    std::vector<uint16_t> vals((size_t)(Mp * ell_cols), 0);
+    for (int64_t br = 0; br < brows; br++) {
+        const std::vector<int32_t> &v = bcols[br];
+        std::copy(v.begin(), v.end(), colidx.begin() + br * width);
+        for (int64_t r = br * block; r < std::min(M, (br + 1) * block); r++)
+            for (int64_t j = A->row_ptr[r]; j < A->row_ptr[r + 1]; j++) {
+                const int32_t c = A->col_idx[j];
+                const int64_t slot = std::lower_bound(v.begin(), v.end(), c / block) - v.begin();
+                const float x = A->val ? A->val[j] : 1.0f;
+                uint16_t h;
+                if (dt == TCASPMM_F16) {
+                    const __half hv = __float2half_rn(x);
+                    std::memcpy(&h, &hv, 2);
+                } else {
+                    const __nv_bfloat16 bv = __float2bfloat16_rn(x);
+                    std::memcpy(&h, &bv, 2);
+                }
+                vals[(size_t)(r * ell_cols + slot * block + c % block)] = h;
+            }
+    }
+    if (ell_bytes) *ell_bytes = (int64_t)(colidx.size() * 4 + vals.size() * 2);
+    cudaStream_t st = (cudaStream_t)stream;
+    int32_t *d_cols = nullptr;
+    void *d_vals = nullptr, *d_Bp = nullptr, *buf = nullptr;
+    float *d_Cp = nullptr;
+    cusparseHandle_t h = nullptr;
+    cusparseSpMatDescr_t Ad = nullptr;
+    cusparseDnMatDescr_t Bd = nullptr, Cd = nullptr;
+    const float alpha = 1.0f, beta = 0.0f;
+    size_t bsz = 0;
+    int rc = CUSPARSE_STATUS_SUCCESS;
+    // Padded B / C when K or M is not a multiple of the block (B rows past K are zero).
+    const bool padB = Kp != K, padC = Mp != M;
+    if (cudaMalloc((void **)&d_cols, colidx.size() * 4) != cudaSuccess ||
+        cudaMalloc(&d_vals, vals.size() * 2) != cudaSuccess ||
+        (padB && cudaMalloc(&d_Bp, (size_t)(Kp * N * 2)) != cudaSuccess) ||
+        (padC && cudaMalloc((void **)&d_Cp, (size_t)(Mp * N * 4)) != cudaSuccess)) {
+        s = bfail(TCASPMM_ERR_ALLOC, "blocked-ELL buffers", 0);
+    } else {
+        cudaMemcpy(d_cols, colidx.data(), colidx.size() * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(d_vals, vals.data(), vals.size() * 2, cudaMemcpyHostToDevice);
+        if (padB) {
+            cudaMemset(d_Bp, 0, (size_t)(Kp * N * 2));
+            cudaMemcpy2D(d_Bp, N * 2, dB, ldb * 2, N * 2, K, cudaMemcpyDeviceToDevice);
+        }
+        if ((rc = cusparseCreate(&h)) != CUSPARSE_STATUS_SUCCESS) {
+            s = bfail(TCASPMM_ERR_CUDA, "cusparseCreate", rc);
+        } else {
+            cusparseSetStream(h, st);
+            rc = cusparseCreateBlockedEll(&Ad, Mp, Kp, block, ell_cols, d_cols, d_vals, CUSPARSE_INDEX_32I,
+                                          CUSPARSE_INDEX_BASE_ZERO, cuda_type(dt));
+            if (rc == CUSPARSE_STATUS_SUCCESS)
+                rc = cusparseCreateDnMat(&Bd, Kp, N, padB ? N : ldb, padB ? d_Bp : (void *)dB, cuda_type(dt),
+                                         CUSPARSE_ORDER_ROW);
+            if (rc == CUSPARSE_STATUS_SUCCESS)
+                rc = cusparseCreateDnMat(&Cd, Mp, N, padC ? N : ldc, padC ? d_Cp : dC, CUDA_R_32F, CUSPARSE_ORDER_ROW);
+            if (rc == CUSPARSE_STATUS_SUCCESS)
+                rc = cusparseSpMM_bufferSize(h, CUSPARSE_OPERATION_NON_TRANSPOSE, CUSPARSE_OPERATION_NON_TRANSPOSE,
+                                             &alpha, Ad, Bd, &beta, Cd, CUDA_R_32F, CUSPARSE_SPMM_ALG_DEFAULT, &bsz);
+            if (rc != CUSPARSE_STATUS_SUCCESS) {
+                s = bfail(TCASPMM_ERR_CUDA, "cusparse blocked-ELL setup", rc);
+            } else if (bsz && cudaMalloc(&buf, bsz) != cudaSuccess) {
+                s = bfail(TCASPMM_ERR_ALLOC, "cusparse workspace", 0);
+            } else {
+                auto run = [&]() {
+                    return cusparseSpMM(h, CUSPARSE_OPERATION_NON_TRANSPOSE, CUSPARSE_OPERATION_NON_TRANSPOSE, &alpha,
+                                        Ad, Bd, &beta, Cd, CUDA_R_32F, CUSPARSE_SPMM_ALG_DEFAULT,
+                                        buf) == CUSPARSE_STATUS_SUCCESS;
+                };
+                s = time_loop(run, warmup, iters, st, ms_per_iter);
+                if (s == TCASPMM_OK && padC)
+                    cudaMemcpy2DAsync(dC, ldc * 4, d_Cp, N * 4, N * 4, M, cudaMemcpyDeviceToDevice, st);
+                cudaStreamSynchronize(st);
+            }
+        }
+    }
+    if (Cd) cusparseDestroyDnMat(Cd);
+    if (Bd) cusparseDestroyDnMat(Bd);
+    if (Ad) cusparseDestroySpMat(Ad);
+    if (h) cusparseDestroy(h);
+    for (void *q : {(void *)d_cols, d_vals, d_Bp, (void *)d_Cp, buf})
+        if (q) cudaFree(q);
     return s;
 }
