@@ -333,7 +333,9 @@ def main():
     h2d = K * N * elem * (world if args.split == "rows" else 1)  # row split: every rank copies all of B
     d2h = M * N * (2 if args.epilogue else 4)
 
-    # ---- cuSPARSE baseline on this rank's block (reported, not a target) ----
+    # ---- library baselines on this rank's block (reported, not targets), timed
+    # with the same L2 protocol as the step above ----
+    T.baselines_set_flush(flush)
     Cs = torch.empty_like(Cd, dtype=torch.float32)
     try:
         ms_cusparse = max_over_ranks(T.cusparse_spmm(plan, Bd, Cs, warmup=3, iters=max(5, min(args.steps, 50)),
@@ -359,6 +361,7 @@ def main():
         Ad[rows, torch.from_numpy(A.col.astype(np.int64)).to(dev)] = torch.from_numpy(A.values()).to(dev).to(tdt)
         Cg = torch.empty_like(Cd)
         gemm = max_over_ranks(T.cublas_gemm(Ad, Bd, Cg, dt, warmup=3, iters=20, stream=stream))
+    T.baselines_set_flush(None)
 
     # ---- CPU baseline (rank 0, N=1 only) ----
     cpu = None
@@ -401,6 +404,8 @@ def main():
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 4)},
             "baselines": {"spmm_cusparse_ms": ms_cusparse, "spmm_cusparse_rel_diff": cs_err,
                           "gemm_cublas_ms": gemm, "spmm_cusparse_blocked_ell": bell,
+                          "timing": "same L2 protocol as value (flushed between calls)" if flush is not None
+                          else "back to back, inputs larger than L2",
                           "spmm_cusparse_gflops": round(flops / (ms_cusparse * 1e-3) / 1e9, 3)
                           if isinstance(ms_cusparse, float) else None},
             "cpu_baseline": cpu,

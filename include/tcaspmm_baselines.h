@@ -12,6 +12,11 @@
 extern "C" {
 #endif
 
+/* Flush L2 between timed calls: before each timed call the baselines write
+ * `bytes` of the device buffer `buf` (larger than L2) and time that call alone;
+ * buf NULL or bytes 0 restores back-to-back timing. */
+void tcaspmm_baselines_set_flush(void *buf, size_t bytes);
+
 /* cusparseSpMM on a device CSR (int32 offsets/indices, values in dt), row-major
  * B (K x N, ld ldb) in dt, fp32 C (M x N, ld ldc), fp32 compute,
  * CUSPARSE_SPMM_ALG_DEFAULT.  Replaces perform_cuSPARSE_SpMM

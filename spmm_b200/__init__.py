@@ -516,7 +516,18 @@ def baselines():
         _blib.tcaspmm_cusparse_blocked_ell.argtypes = [_P(_CSR), C.c_int, _vp, _i64, _vp, _i64, _i64, C.c_int,
                                                        C.c_int, C.c_int, _vp, _P(C.c_double), _P(_i64)]
         _blib.tcaspmm_cusparse_blocked_ell.restype = C.c_int
+        _blib.tcaspmm_baselines_set_flush.argtypes = [_vp, C.c_size_t]
+        _blib.tcaspmm_baselines_set_flush.restype = None
     return _blib
+
+
+def baselines_set_flush(buf) -> None:
+    """Flush L2 by writing `buf` (a device tensor larger than L2) before every timed baseline call;
+    None restores back-to-back timing."""
+    if buf is None:
+        baselines().tcaspmm_baselines_set_flush(None, 0)
+    else:
+        baselines().tcaspmm_baselines_set_flush(_ptr(buf), buf.numel() * buf.element_size())
 
 
 def cusparse_blocked_ell(A: CSR, block: int, B, Cout, dt, warmup: int = 5, iters: int = 10, stream=None):

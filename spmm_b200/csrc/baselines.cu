@@ -30,6 +30,11 @@ cudaDataType_t cuda_type(tcaspmm_dtype dt)
     return dt == TCASPMM_F32 ? CUDA_R_32F : dt == TCASPMM_F16 ? CUDA_R_16F : CUDA_R_16BF;
 }
 
+// L2 flush between timed calls (set by tcaspmm_baselines_set_flush): the same
+// protocol bench.py uses for tcaspmm on inputs smaller than L2.
+void *g_flush = nullptr;
+size_t g_flush_bytes = 0;
+
 template <typename F>
 tcaspmm_status time_loop(F &&f, int warmup, int iters, cudaStream_t st, double *ms)
 {
@@ -38,13 +43,27 @@ tcaspmm_status time_loop(F &&f, int warmup, int iters, cudaStream_t st, double *
     cudaEvent_t a, b;
     cudaEventCreate(&a);
     cudaEventCreate(&b);
-    cudaEventRecord(a, st);
     bool ok = true;
-    for (int i = 0; i < iters && ok; i++) ok = f();
-    cudaEventRecord(b, st);
-    cudaEventSynchronize(b);
     float t = 0.0f;
-    cudaEventElapsedTime(&t, a, b);
+    if (g_flush) {
+        // Per call: flush, then events around the call alone.
+        for (int i = 0; i < iters && ok; i++) {
+            cudaMemsetAsync(g_flush, i & 0xff, g_flush_bytes, st);
+            cudaEventRecord(a, st);
+            ok = f();
+            cudaEventRecord(b, st);
+            cudaEventSynchronize(b);
+            float ti = 0.0f;
+            cudaEventElapsedTime(&ti, a, b);
+            t += ti;
+        }
+    } else {
+        cudaEventRecord(a, st);
+        for (int i = 0; i < iters && ok; i++) ok = f();
+        cudaEventRecord(b, st);
+        cudaEventSynchronize(b);
+        cudaEventElapsedTime(&t, a, b);
+    }
     cudaEventDestroy(a);
     cudaEventDestroy(b);
     cudaError_t e = cudaGetLastError();
@@ -54,6 +73,12 @@ tcaspmm_status time_loop(F &&f, int warmup, int iters, cudaStream_t st, double *
 }
 
 }  // namespace
+
+extern "C" void tcaspmm_baselines_set_flush(void *buf, size_t bytes)
+{
+    g_flush = bytes ? buf : nullptr;
+    g_flush_bytes = bytes;
+}
 
 extern "C" tcaspmm_status tcaspmm_cusparse_spmm(const int32_t *d_row_ptr, const int32_t *d_col, const void *d_val,
                                                 int64_t M, int64_t K, int64_t nnz, const void *dB, int64_t ldb,

@@ -47,6 +47,12 @@ struct Shard {
     mutable bool maps_valid = false;
     mutable const void *maps_ptr = nullptr;
     mutable int64_t maps_ldb = 0;
+    // Tensor map over the last C block written by bulk stores (one CUtensorMap).
+    alignas(64) mutable unsigned char cmap[128] = {};
+    mutable bool cmap_valid = false;
+    mutable const void *cmap_ptr = nullptr;
+    mutable int64_t cmap_ldc = 0;
+    mutable int cmap_out = 0;
 
     int *err = nullptr;  // device error word (bounded waits that ran out)
 };

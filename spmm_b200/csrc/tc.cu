@@ -67,6 +67,7 @@ constexpr int VAL_BYTES = R * KT * 2;                  // 1 KB of values per til
 constexpr int STAGE_BYTES = PANEL_BYTES + TPS * VAL_BYTES;
 constexpr int TMEM_COLS = 2 * R;  // two accumulators
 constexpr int NUM_THREADS = 192;
+constexpr int CBUF_BYTES = 4 * 32 * 32 * 4;  // C staging: a 32 x 32 fp32 tile per epilogue warp
 constexpr int EPI_THREADS = 128;
 constexpr unsigned long long WAIT_CYCLES = 4ull << 30;  // ~2 s at 2 GHz: no legitimate wait comes close
 static_assert(IDX_TILES % TPS == 0, "stages must not straddle index refills");
@@ -87,6 +88,7 @@ struct TcParams {
     int stall_test;          // self-test: the producer issues no copies, so waits must time out
     int has_ep;              // apply `ep` (row scale, bias, ReLU, 16-bit C)
     EpiParams ep;
+    int tma_store;           // C written by bulk tensor stores through `cmap` (aligned C)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -163,6 +165,19 @@ __device__ __forceinline__ void bulk_copy(uint32_t dst, const void *src, uint32_
                  "l"(src), "r"(bytes), "r"(bar)
                  : "memory");
 }
+
+// 2-D bulk tensor store of the box at (x, y) of tmap from shared memory, and
+// its bulk-group bookkeeping (per issuing thread).
+__device__ __forceinline__ void tma_store_2d(const void *tmap, int x, int y, uint32_t src)
+{
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(tmap), "r"(x),
+                 "r"(y), "r"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout)
 {
@@ -260,13 +275,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
 }
 
 template <bool BF16>
-__global__ void __launch_bounds__(NUM_THREADS, 1) tc_kernel(const TcParams p, const __grid_constant__ BMaps maps)
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    tc_kernel(const TcParams p, const __grid_constant__ BMaps maps, const __grid_constant__ CUtensorMap cmap)
 {
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte aligned stage ring, then the index buffer and the barriers.
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    int32_t *idxbuf = (int32_t *)(smem + STAGES * STAGE_BYTES);  // [IDX_TILES][KT]
-    uint64_t *bars = (uint64_t *)(smem + STAGES * STAGE_BYTES + IDX_TILES * KT * 4);
+    uint8_t *cbuf = smem + STAGES * STAGE_BYTES;                             // [4 warps][32 rows][32 columns]
+    int32_t *idxbuf = (int32_t *)(smem + STAGES * STAGE_BYTES + CBUF_BYTES);  // [IDX_TILES][KT]
+    uint64_t *bars = (uint64_t *)(smem + STAGES * STAGE_BYTES + CBUF_BYTES + IDX_TILES * KT * 4);
     uint64_t *full = bars;                  // [STAGES] producer -> MMA
     uint64_t *empty = bars + STAGES;        // [STAGES] MMA -> producer
     uint64_t *accf = bars + 2 * STAGES;     // [2] MMA -> epilogue
@@ -449,8 +466,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_kernel(const TcParams p, co
 #pragma unroll
                 for (int r = 0; r < R; ++r) v[r] *= __shfl_sync(0xffffffffu, sc, r);
             }
-            const int f = (u % p.nfb) * MB + warp * 32 + lane;
-            if (f < p.ncols) {
+            const int x = (u % p.nfb) * MB + warp * 32;  // this warp's first output column
+            const int f = x + lane;
+            if (p.tma_store) {
+                // Stage the warp's 32 x 32 tile in shared memory (row r at
+                // 32 r elements, conflict-free), then one bulk tensor store; the
+                // tensor map clips rows past the block's end and columns past N.
+                if (x < p.ncols) {  // warp-uniform
+                    if (lane == 0) bulk_wait_read();  // the previous store has read the buffer
+                    __syncwarp();
+                    uint8_t *cw = cbuf + warp * 4096;
+                    if (!p.has_ep) {
+#pragma unroll
+                        for (int r = 0; r < R; ++r) reinterpret_cast<float *>(cw)[r * 32 + lane] = v[r];
+                    } else {
+                        const float b = (p.ep.bias && f < p.ncols) ? __ldg(p.ep.bias + f) : 0.0f;
+#pragma unroll
+                        for (int r = 0; r < R; ++r) {
+                            float y = v[r] + b;
+                            if (p.ep.relu) y = fmaxf(y, 0.0f);
+                            if (p.ep.out == 0)
+                                reinterpret_cast<float *>(cw)[r * 32 + lane] = y;
+                            else if (p.ep.out == 1)
+                                reinterpret_cast<__half *>(cw)[r * 32 + lane] = __float2half_rn(y);
+                            else
+                                reinterpret_cast<__nv_bfloat16 *>(cw)[r * 32 + lane] = __float2bfloat16_rn(y);
+                        }
+                    }
+                    fence_proxy_async();  // generic-proxy writes -> visible to the bulk copy
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&cmap, x, w.x, smem_u32(cw));
+                        bulk_commit();
+                    }
+                }
+            } else if (f < p.ncols) {
                 if (!p.has_ep) {
                     float *c = static_cast<float *>(p.C) + (long long)w.x * p.ldc + f;
 #pragma unroll
@@ -461,6 +511,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_kernel(const TcParams p, co
                 }
             }
         }
+        if (p.tma_store && lane == 0) bulk_wait_all();  // C is written before the CTA exits
     }
 
     tc_fence_before();
@@ -473,7 +524,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_kernel(const TcParams p, co
 
 // Tail: 2 * STAGES + 5 mbarriers, the TMEM address and the abort flag.
 constexpr size_t kBarBytes = (2 * STAGES + 5) * 8 + 8;
-constexpr size_t kSmemBytes = 1024 + STAGES * STAGE_BYTES + IDX_TILES * KT * 4 + (kBarBytes + 127) / 128 * 128;  // ~85 KB
+constexpr size_t kSmemBytes =
+    1024 + STAGES * STAGE_BYTES + CBUF_BYTES + IDX_TILES * KT * 4 + (kBarBytes + 127) / 128 * 128;  // ~101 KB
 
 template <typename X>
 tcaspmm_status upload_vec(Shard *sh, X **dst, const std::vector<X> &v, const char *what)
@@ -533,7 +585,7 @@ tcaspmm_status encode_b_maps(tcaspmm_dtype dt, const void *dB, int64_t ncols, in
     return r == CUDA_SUCCESS ? TCASPMM_OK : fail(TCASPMM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
 }
 
-static_assert(sizeof(BMaps) <= sizeof(Shard::maps), "tensor-map storage in Shard");
+static_assert(sizeof(BMaps) <= sizeof(Shard::maps) && sizeof(CUtensorMap) <= sizeof(Shard::cmap), "tensor-map storage in Shard");
 
 template <bool BF16>
 cudaError_t smem_optin()
@@ -541,12 +593,30 @@ cudaError_t smem_optin()
     return cudaFuncSetAttribute(tc_kernel<BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
 }
 
-void launch_kernel(bool bf16, int grid, const TcParams &p, const BMaps &maps, cudaStream_t st)
+void launch_kernel(bool bf16, int grid, const TcParams &p, const BMaps &maps, const CUtensorMap &cmap, cudaStream_t st)
 {
     if (bf16)
-        tc_kernel<true><<<grid, NUM_THREADS, kSmemBytes, st>>>(p, maps);
+        tc_kernel<true><<<grid, NUM_THREADS, kSmemBytes, st>>>(p, maps, cmap);
     else
-        tc_kernel<false><<<grid, NUM_THREADS, kSmemBytes, st>>>(p, maps);
+        tc_kernel<false><<<grid, NUM_THREADS, kSmemBytes, st>>>(p, maps, cmap);
+}
+
+// Tensor map over a C block of ncols x rows elements of the output type (ldc
+// elements per row), box 32 x 32, no swizzle: the epilogue's bulk stores.
+tcaspmm_status encode_c_map(int out, void *dC, int64_t ncols, int64_t rows, int64_t ldc, CUtensorMap *m)
+{
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(TCASPMM_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const int esize = out == 0 ? 4 : 2;
+    const cuuint64_t dims[2] = {(cuuint64_t)ncols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)(ldc * esize)};
+    const cuuint32_t box[2] = {32, 32}, estr[2] = {1, 1};
+    const CUtensorMapDataType ty = out == 0   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : out == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const CUresult r = fn(m, ty, 2, dC, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? TCASPMM_OK : fail(TCASPMM_ERR_CUDA, "cuTensorMapEncodeTiled (C) failed (%d)", (int)r);
 }
 
 }  // namespace
@@ -624,6 +694,20 @@ tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int6
     p.stall_test = 0;
     p.has_ep = ep != nullptr;
     p.ep = ep ? EpiParams{ep->row_scale, ep->bias, ep->relu, ep->out} : EpiParams{nullptr, nullptr, 0, 0};
+    // Bulk tensor stores of C need a 16-byte aligned C with 16-byte row pitch;
+    // the C tensor map is rebuilt only when C, its pitch or its type change.
+    const int out = ep ? ep->out : 0;
+    const int esize = out == 0 ? 4 : 2;
+    p.tma_store = ((uintptr_t)dC % 16 == 0) && ((ldc * esize) % 16 == 0);
+    if (p.tma_store && !(sh.cmap_valid && sh.cmap_ptr == dC && sh.cmap_ldc == ldc && sh.cmap_out == out)) {
+        sh.cmap_valid = false;
+        tcaspmm_status ms = encode_c_map(out, dC, sh.ncols, sh.nrows, ldc, (CUtensorMap *)sh.cmap);
+        if (ms != TCASPMM_OK) return ms;
+        sh.cmap_valid = true;
+        sh.cmap_ptr = dC;
+        sh.cmap_ldc = ldc;
+        sh.cmap_out = out;
+    }
     const int grid = std::min(p.n_units, sh.tc_ctas_per_sm * sh.num_sms);  // persistent
     // Tensor maps depend on the B block: rebuilt only when it changes.
     if (!(sh.maps_valid && sh.maps_ptr == dB && sh.maps_ldb == ldb)) {
@@ -634,7 +718,7 @@ tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int6
         sh.maps_ptr = dB;
         sh.maps_ldb = ldb;
     }
-    launch_kernel(dt == TCASPMM_BF16, grid, p, *(const BMaps *)sh.maps, st);
+    launch_kernel(dt == TCASPMM_BF16, grid, p, *(const BMaps *)sh.maps, *(const CUtensorMap *)sh.cmap, st);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TCASPMM_OK : cuda_fail(e, "tc kernel launch");
 }
@@ -695,9 +779,10 @@ extern "C" tcaspmm_status tcaspmm_selftest_tc_timeout(int device, unsigned long 
         p.stall_test = 1;
         p.has_ep = 0;
         p.ep = EpiParams{nullptr, nullptr, 0, 0};
+        p.tma_store = 0;
         e = smem_optin<false>();
         if (e == cudaSuccess) {
-            launch_kernel(false, 1, p, maps, 0);
+            launch_kernel(false, 1, p, maps, CUtensorMap{}, 0);
             e = cudaGetLastError();
         }
         if (e == cudaSuccess) e = cudaDeviceSynchronize();
