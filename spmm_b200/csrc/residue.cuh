@@ -295,10 +295,15 @@ __device__ __forceinline__ void stream_lean(const ResidueParams &p, int r_lo, in
         Raw<T, VEC> rb[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) load_raw<T, VEC>(B + (long long)cc[u] * p.ldb, rb[u]);
+        if (j + U <= e) {  // the whole chunk lies in the current row: no row-end checks
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            pass_row_ends(j + u);
-            fma_raw<T, VEC>(vv[u], rb[u], acc);
+            for (int u = 0; u < U; ++u) fma_raw<T, VEC>(vv[u], rb[u], acc);
+        } else {
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                pass_row_ends(j + u);
+                fma_raw<T, VEC>(vv[u], rb[u], acc);
+            }
         }
     }
     for (; j < jend; ++j) {
@@ -331,10 +336,10 @@ __device__ __forceinline__ int first_row_at(const int32_t *row_ptr, int lo, int 
 
 // 256 threads, register budget for 4 resident blocks per SM (64 registers):
 // measured faster than 40 registers / 6 blocks and than 80 / 3 on GCN, SAGE and
-// the skew config.  The epilogue instantiations get 3 blocks (80 registers) so
-// the epilogue's live values do not spill the nonzero stream.
+// the skew config, the epilogue instantiations included (at 80 registers they
+// ran 25% slower on GCN for the lost occupancy).
 template <typename T, int VEC, int G, int U, bool EPI>
-__global__ void __launch_bounds__(256, EPI ? 3 : 4) residue_kernel(const ResidueParams p)
+__global__ void __launch_bounds__(256, 4) residue_kernel(const ResidueParams p)
 {
     constexpr int P = 32 / G;
     constexpr int CPP = G * VEC;  // columns per pass
