@@ -38,6 +38,7 @@ struct Shard {
     int num_sms = 148;
     int tc_ctas_per_sm = 1;       // resident tc-kernel CTAs per SM (persistent grid)
     Int4 *tc_windows = nullptr;   // {first row, first tile, tiles, rows}, by decreasing tile count
+    int32_t *tc_dense = nullptr;  // per window: first column of its consecutive run, or -1
     int32_t *tc_cols = nullptr;   // KT B-row indices per tile
     void *tc_vals = nullptr;      // R x KT values per tile, shared-memory image
     Int2 *tc_fallback = nullptr;  // one row range per window (unaligned B: CUDA cores)

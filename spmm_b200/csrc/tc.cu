@@ -74,6 +74,7 @@ static_assert(IDX_TILES % TPS == 0, "stages must not straddle index refills");
 
 struct TcParams {
     const int4 *windows;     // {first row, first tile, tiles, rows}, by decreasing tile count
+    const int32_t *dense_c0; // per window: first column when its columns are one consecutive run, else -1
     const int32_t *tile_cols;
     const uint16_t *tile_vals;
     const void *B;
@@ -295,6 +296,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
+    // The producer's first window descriptor, loaded before the set-up barrier so
+    // its latency overlaps the barrier initialisation and the TMEM allocation.
+    int4 w_first = make_int4(0, 0, 0, 0);
+    int c_first = -1;
+    if (warp == 5 && (int)blockIdx.x < p.n_units) {
+        w_first = p.windows[blockIdx.x / p.nfb];
+        c_first = p.dense_c0[blockIdx.x / p.nfb];
+    }
 
     if (tid == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -338,10 +347,44 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
             const int win = u / p.nfb;
-            const int4 w = p.windows[win];
+            const bool first = u == (int)blockIdx.x;
+            const int4 w = first ? w_first : p.windows[win];
+            const int c0 = first ? c_first : p.dense_c0[win];
             const int n0 = (u % p.nfb) * MB;
             const int nst = (w.z + TPS - 1) / TPS;  // stages of this unit (w.z >= 1)
             const int rot = win % nst;
+            if (c0 >= 0) {
+                // One consecutive run of columns c0, c0 + 1, ...: tile t covers B
+                // rows c0 + 16 t .. + 15 (rows past the run have zero values, rows
+                // past K are zero-filled by TMA), so no indices are loaded.
+                for (int k = 0; ok && k < nst; ++k, ++g) {
+                    const int t = stage_at(k, rot, nst) * TPS;
+                    const int s = g % STAGES;
+                    const int n = min(TPS, w.z - t);
+                    ok = __all_sync(0xffffffffu, wait_bounded(smem_u32(&empty[s]), ((g / STAGES) & 1) ^ 1,
+                                                              abort_flag, p.err, 1, p.wait_cycles));
+                    if (!ok) break;
+                    if (lane == 0 && !p.stall_test) {
+                        const uint32_t fb = smem_u32(&full[s]);
+                        const uint32_t panel = smem_u32(smem + s * STAGE_BYTES);
+                        const int y = c0 + t * KT;
+                        mbar_expect_tx(fb, (uint32_t)n * (TILE_PANEL_BYTES + VAL_BYTES));
+                        if (n == TPS) {
+                            tma_box(panel, tm_64, n0, y, fb);
+                            tma_box(panel + HALF_BYTES, tm_64, n0 + 64, y, fb);
+                        } else {
+                            for (int j = 0; j < n; ++j) {
+                                const uint32_t tp = panel + j * TILE_PANEL_BYTES / 2;
+                                tma_box(tp, tm_16, n0, y + j * KT, fb);
+                                tma_box(tp + HALF_BYTES, tm_16, n0 + 64, y + j * KT, fb);
+                            }
+                        }
+                        bulk_copy(panel + PANEL_BYTES, p.tile_vals + ((long long)w.y + t) * (R * KT),
+                                  (uint32_t)n * VAL_BYTES, fb);
+                    }
+                }
+                continue;
+            }
             int chunk = -1;  // IDX_TILES-tile chunk whose indices are staged
             for (int k = 0; ok && k < nst; ++k, ++g) {
                 const int t = stage_at(k, rot, nst) * TPS;  // first tile of the stage
@@ -649,12 +692,27 @@ tcaspmm_status tc_upload(const tcaspmm_csr &, tcaspmm_dtype dt, Shard *sh)
                 img[t * R * KT + (n / 8) * 128 + (k / 8) * 64 + (n % 8) * 8 + (k % 8)] =
                     dt == TCASPMM_BF16 ? float_to_bf16_bits(v) : float_to_half_bits(v);
             }
+    // Windows whose columns are one consecutive run (padding repeats the last
+    // column) need no index loads: their tiles are boxes of consecutive B rows.
+    // Only when K >= 64, so that the 64- and 16-row boxes are never clipped.
+    std::vector<int32_t> dense(windows.size(), -1);
+    for (size_t i = 0; i < windows.size() && sh->K >= TPS * KT; i++) {
+        const int32_t *c = T.tile_cols.data() + (size_t)windows[i].y * KT;
+        const int64_t n = (int64_t)windows[i].z * KT;
+        bool ok = true;
+        int64_t q = 1;
+        for (; q < n && c[q] == c[0] + q; q++) {
+        }
+        for (; q < n && ok; q++) ok = c[q] == c[q - 1];  // padding
+        if (ok) dense[i] = c[0];
+    }
     // Fallback row ranges over tc rows (run on the CUDA cores when B or C is
     // not 16-byte aligned at execute time).
     std::vector<Int2> fb;
     for (const Int4 &w : T.windows) fb.push_back(Int2{w.x, w.x + w.w});
     tcaspmm_status s;
     if ((s = upload_vec(sh, &sh->tc_windows, windows, "tc windows")) != TCASPMM_OK) return s;
+    if ((s = upload_vec(sh, &sh->tc_dense, dense, "tc dense runs")) != TCASPMM_OK) return s;
     if ((s = upload_vec(sh, &sh->tc_cols, T.tile_cols, "tc columns")) != TCASPMM_OK) return s;
     if ((s = upload_vec(sh, (uint16_t **)&sh->tc_vals, img, "tc values")) != TCASPMM_OK) return s;
     if ((s = upload_vec(sh, &sh->tc_fallback, fb, "tc fallback ranges")) != TCASPMM_OK) return s;
@@ -680,6 +738,7 @@ tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int6
         return launch_residue(sh, dt, dB, ldb, dC, ldc, ep, st, sh.tc_fallback, sh.n_windows);
     TcParams p;
     p.windows = (const int4 *)sh.tc_windows;
+    p.dense_c0 = sh.tc_dense;
     p.tile_cols = sh.tc_cols;
     p.tile_vals = (const uint16_t *)sh.tc_vals;
     p.B = dB;
@@ -741,13 +800,15 @@ extern "C" tcaspmm_status tcaspmm_selftest_tc_timeout(int device, unsigned long 
     const int4 win = make_int4(0, 0, 1, R);
     const std::vector<int32_t> cols(KT, 0);
     const std::vector<uint16_t> vals(R * KT, 0);
-    void *d_win = nullptr, *d_cols = nullptr, *d_vals = nullptr, *d_b = nullptr, *d_c = nullptr;
+    const int32_t no_run = -1;
+    void *d_win = nullptr, *d_dense = nullptr, *d_cols = nullptr, *d_vals = nullptr, *d_b = nullptr, *d_c = nullptr;
     int *d_err = nullptr;
     tcaspmm_status st = TCASPMM_OK;
     auto alloc = [&](void **ptr, size_t n) {
         if (st == TCASPMM_OK && (e = cudaMalloc(ptr, n)) != cudaSuccess) st = cuda_fail(e, "self-test allocation");
     };
     alloc(&d_win, sizeof(win));
+    alloc(&d_dense, sizeof(no_run));
     alloc(&d_cols, cols.size() * 4);
     alloc(&d_vals, vals.size() * 2);
     alloc(&d_b, TPS * KT * MB * 2);
@@ -756,6 +817,7 @@ extern "C" tcaspmm_status tcaspmm_selftest_tc_timeout(int device, unsigned long 
     BMaps maps;
     if (st == TCASPMM_OK) {
         cudaMemcpy(d_win, &win, sizeof(win), cudaMemcpyHostToDevice);
+        cudaMemcpy(d_dense, &no_run, sizeof(no_run), cudaMemcpyHostToDevice);
         cudaMemcpy(d_cols, cols.data(), cols.size() * 4, cudaMemcpyHostToDevice);
         cudaMemcpy(d_vals, vals.data(), vals.size() * 2, cudaMemcpyHostToDevice);
         cudaMemset(d_b, 0, TPS * KT * MB * 2);
@@ -765,6 +827,7 @@ extern "C" tcaspmm_status tcaspmm_selftest_tc_timeout(int device, unsigned long 
     if (st == TCASPMM_OK) {
         TcParams p;
         p.windows = (const int4 *)d_win;
+        p.dense_c0 = (const int32_t *)d_dense;
         p.tile_cols = (const int32_t *)d_cols;
         p.tile_vals = (const uint16_t *)d_vals;
         p.B = d_b;
@@ -796,7 +859,7 @@ extern "C" tcaspmm_status tcaspmm_selftest_tc_timeout(int device, unsigned long 
                      : fail(TCASPMM_OK, "no time-out recorded");
         }
     }
-    for (void *ptr : {d_win, d_cols, d_vals, d_b, d_c, (void *)d_err})
+    for (void *ptr : {d_win, d_dense, d_cols, d_vals, d_b, d_c, (void *)d_err})
         if (ptr) cudaFree(ptr);
     return st;
 }

@@ -291,8 +291,9 @@ def _window_union_matrix(unions, K, seed=21, drop=0.1):
 
 def test_tensor_core_stage_shapes_bit_exact():
     """Every producer form: 64-row boxes, 16-row boxes, gather4 tiles, partial stages,
-    index refills past 32 tiles, and a padded last tile whose span looks like 16
-    consecutive rows ({.., 40, 55, 55, ..}) but is not."""
+    index refills past 32 tiles, a padded last tile whose span looks like 16
+    consecutive rows ({.., 40, 55, 55, ..}) but is not, and windows whose columns
+    are one consecutive run (loaded without tile indices, boxes reaching past K)."""
     K = 2048
     unions = [
         list(range(32)) + [40, 55],                                   # padded tile of span 15
@@ -301,6 +302,8 @@ def test_tensor_core_stage_shapes_bit_exact():
         list(range(0, K, 2)),                                         # 64 gathered tiles, two index refills
         list(range(1024)),                                            # 16 stages of 64 consecutive rows
         list(range(1000, 1016)) + list(range(1017, 1033)),            # 16-row box, then a 16-span gap tile
+        list(range(100, 140)),                                        # one run: 3 tiles, padded, no indices
+        list(range(K - 20, K)),                                       # one run ending at K: boxes past K
     ]
     A = _window_union_matrix(unions, K)
     B = np.round(T.gen_dense(K, 256, 5, "f32") * 4).astype(np.float32)
