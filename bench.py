@@ -213,6 +213,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--epilogue", action="store_true",
                     help="fused epilogue: C = relu(row_scale * (A B) + bias) stored as bf16")
+    ap.add_argument("--gather", action="store_true",
+                    help="also time the step followed by an NCCL all-gather of C (N > 1)")
     ap.add_argument("--split", default="columns", choices=["columns", "rows"],
                     help="multi-GPU partition: column blocks of B/C (A replicated) or row blocks of A/C "
                          "(B replicated)")
@@ -316,6 +318,41 @@ def main():
     flops = 2.0 * nnz * N
     value = flops / (ms_step * 1e-3) / 1e9
 
+    # ---- optional: the step followed by the all-gather of C over NVLink (NCCL), so
+    # every rank holds the whole M x N product; reported beside value, not in it ----
+    gather = None
+    if args.gather and world > 1:
+        if args.split == "rows":
+            counts = [None] * world
+            dist.all_gather_object(counts, int(mrows))
+            Cfull = torch.empty((world, max(counts), ncols), dtype=Cd.dtype, device=dev)  # row blocks, padded
+            parts = list(Cfull.unbind(0))
+        else:
+            b0 = T.partition_columns(N, dt, world, 0)[1]  # block width (the last block may be narrower)
+            Cfull = torch.empty((world, M, b0), dtype=Cd.dtype, device=dev)
+            parts = list(Cfull.unbind(0))
+        Cpad = torch.zeros(parts[rank].shape, dtype=Cd.dtype, device=dev)
+
+        Cview = Cpad[:mrows, :ncols]
+
+        def gathered_step():
+            plan.execute1(Bd, Cview, stream, epilogue=ep)  # straight into the send buffer
+            dist.all_gather(parts, Cpad)
+
+        for _ in range(3):
+            gathered_step()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        gsteps = max(5, min(args.steps, 50))
+        e0.record(stream)
+        for _ in range(gsteps):
+            gathered_step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        gms = max_over_ranks(e0.elapsed_time(e1) / gsteps)
+        gather = {"ms_per_step": round(gms, 5), "collective": "all_gather of C blocks (NCCL)",
+                  "bytes_per_rank": int(M * N * Cd.element_size())}
+
     # ---- end to end through the public API: pinned host B -> device, execute, C -> pinned host ----
     Bpin = Bh.pin_memory()
     Cpin = torch.empty((mrows, ncols), dtype=cdt).pin_memory()
@@ -409,6 +446,7 @@ def main():
                           "spmm_cusparse_gflops": round(flops / (ms_cusparse * 1e-3) / 1e9, 3)
                           if isinstance(ms_cusparse, float) else None},
             "cpu_baseline": cpu,
+            **({"with_gather": gather} if gather else {}),
             "clocks": sampler.summary(),
             "gpu_launches": kernels_per_step * args.steps * world,
         }
