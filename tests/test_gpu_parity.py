@@ -225,6 +225,18 @@ def test_tensor_core_integer_values_bit_exact():
     np.testing.assert_array_equal(out, reference(A, B, "f16").astype(np.float32))
 
 
+@pytest.mark.parametrize("K", [12, 40, 64, 70])
+def test_tensor_core_windows_with_few_b_rows(K):
+    """K below the 16- and 64-row TMA boxes: the boxes are clipped to K and only
+    the forms that fit are issued (no index-free runs below K = 64)."""
+    A = T.gen_uniform(256, K, 0.6, K)
+    A = T.CSR(A.nrow, A.ncol, A.row_ptr, A.col, np.round(A.val * 4).astype(np.float32))
+    B = np.round(T.gen_dense(K, 64, 3, "f32") * 4).astype(np.float32)
+    out, st = run(A, B, "f16")
+    assert st["tc_windows"] > 0
+    np.testing.assert_array_equal(out, reference(A, B, "f16").astype(np.float32))
+
+
 @pytest.mark.parametrize("dt", ["f32", "f16"])
 def test_row_split_plan_on_one_device(dt):
     """Row-split plan with two shards placed on cuda:0: each shard writes its row
