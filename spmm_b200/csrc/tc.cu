@@ -66,7 +66,8 @@ constexpr int HALF_BYTES = PANEL_BYTES / 2;            // one 64-column half: 8 
 constexpr int VAL_BYTES = R * KT * 2;                  // 1 KB of values per tile
 constexpr int STAGE_BYTES = PANEL_BYTES + TPS * VAL_BYTES;
 constexpr int TMEM_COLS = 2 * R;  // two accumulators
-constexpr int NUM_THREADS = 192;
+constexpr int NPROD = 2;  // producer warps, taking stages round-robin
+constexpr int NUM_THREADS = 160 + 32 * NPROD;
 constexpr int CBUF_BYTES = 4 * 32 * 32 * 4;  // C staging: a 32 x 32 fp32 tile per epilogue warp
 constexpr int EPI_THREADS = 128;
 constexpr unsigned long long WAIT_CYCLES = 4ull << 30;  // ~2 s at 2 GHz: no legitimate wait comes close
@@ -283,8 +284,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // 1024-byte aligned stage ring, then the index buffer and the barriers.
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *cbuf = smem + STAGES * STAGE_BYTES;                             // [4 warps][32 rows][32 columns]
-    int32_t *idxbuf = (int32_t *)(smem + STAGES * STAGE_BYTES + CBUF_BYTES);  // [IDX_TILES][KT]
-    uint64_t *bars = (uint64_t *)(smem + STAGES * STAGE_BYTES + CBUF_BYTES + IDX_TILES * KT * 4);
+    int32_t *idxbuf = (int32_t *)(smem + STAGES * STAGE_BYTES + CBUF_BYTES);  // [NPROD][IDX_TILES][KT]
+    uint64_t *bars = (uint64_t *)(smem + STAGES * STAGE_BYTES + CBUF_BYTES + NPROD * IDX_TILES * KT * 4);
     uint64_t *full = bars;                  // [STAGES] producer -> MMA
     uint64_t *empty = bars + STAGES;        // [STAGES] MMA -> producer
     uint64_t *accf = bars + 2 * STAGES;     // [2] MMA -> epilogue
@@ -300,7 +301,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // its latency overlaps the barrier initialisation and the TMEM allocation.
     int4 w_first = make_int4(0, 0, 0, 0);
     int c_first = -1;
-    if (warp == 5 && (int)blockIdx.x < p.n_units) {
+    if (warp >= 5 && (int)blockIdx.x < p.n_units) {
         w_first = p.windows[blockIdx.x / p.nfb];
         c_first = p.dense_c0[blockIdx.x / p.nfb];
     }
@@ -329,15 +330,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
 
-    if (warp == 5) {
-        // ------------------------------ producer -------------------------------
+    if (warp >= 5) {
+        // ------------------------------ producers ------------------------------
+        // Warps 5 .. 5 + NPROD - 1 walk the same stage sequence; warp 5 + i
+        // fills the stages g with g % NPROD == i (one TMA issuer per warp).
         // The warp stages the B-row indices of up to IDX_TILES tiles in shared
         // memory with one coalesced load; lane 0 then fills one stage per TPS
         // tiles: one 64 x 64 box per column half when the stage's 64 B rows are
         // consecutive, else per tile a 64 x 16 box (16 consecutive rows) or four
         // gather4 loads, plus one bulk copy of the stage's value tiles.  Abort
         // decisions are warp-uniform.
-        uint32_t g = 0;  // stages issued by this CTA
+        const int pw = warp - 5;
+        int32_t *myidx = idxbuf + pw * IDX_TILES * KT;
+        uint32_t g = 0;  // stages of this CTA (issued by this warp or the other producers)
         bool ok = true;
         const void *tm_g = &maps.gather, *tm_16 = &maps.box16, *tm_64 = &maps.box64;
         if (lane == 0) {
@@ -358,6 +363,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 // rows c0 + 16 t .. + 15 (rows past the run have zero values, rows
                 // past K are zero-filled by TMA), so no indices are loaded.
                 for (int k = 0; ok && k < nst; ++k, ++g) {
+                    if ((int)(g % NPROD) != pw) continue;
                     const int t = stage_at(k, rot, nst) * TPS;
                     const int s = g % STAGES;
                     const int n = min(TPS, w.z - t);
@@ -393,9 +399,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const int t0 = chunk * IDX_TILES, nt = min(IDX_TILES, w.z - t0);
                     __syncwarp();  // previous indices consumed
                     for (int q = lane; q < nt * KT; q += 32)
-                        idxbuf[q] = __ldg(p.tile_cols + ((long long)w.y + t0) * KT + q);
+                        myidx[q] = __ldg(p.tile_cols + ((long long)w.y + t0) * KT + q);
                     __syncwarp();  // indices visible to the warp
                 }
+                if ((int)(g % NPROD) != pw) continue;
                 const int s = g % STAGES;
                 const int n = min(TPS, w.z - t);  // tiles in this stage
                 ok = __all_sync(0xffffffffu, wait_bounded(smem_u32(&empty[s]), ((g / STAGES) & 1) ^ 1, abort_flag,
@@ -404,7 +411,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (lane == 0 && !p.stall_test) {
                     const uint32_t fb = smem_u32(&full[s]);
                     const uint32_t panel = smem_u32(smem + s * STAGE_BYTES);
-                    const int32_t *ix = idxbuf + (t - chunk * IDX_TILES) * KT;
+                    const int32_t *ix = myidx + (t - chunk * IDX_TILES) * KT;
                     mbar_expect_tx(fb, (uint32_t)n * (TILE_PANEL_BYTES + VAL_BYTES));
                     // A window's columns ascend, distinct except the padding of
                     // its last tile, which repeats the last column.  So m
@@ -441,7 +448,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0 && !p.stall_test) {
             int no_abort = 0;
             for (uint32_t k = g > (uint32_t)STAGES ? g - STAGES : 0; k < g; ++k)
-                wait_bounded(smem_u32(&full[k % STAGES]), (k / STAGES) & 1, (volatile int *)&no_abort, p.err, 16,
+                if ((int)(k % NPROD) == pw)
+                    wait_bounded(smem_u32(&full[k % STAGES]), (k / STAGES) & 1, (volatile int *)&no_abort, p.err, 16,
                              p.wait_cycles);
         }
         __syncwarp();
@@ -568,7 +576,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // Tail: 2 * STAGES + 5 mbarriers, the TMEM address and the abort flag.
 constexpr size_t kBarBytes = (2 * STAGES + 5) * 8 + 8;
 constexpr size_t kSmemBytes =
-    1024 + STAGES * STAGE_BYTES + CBUF_BYTES + IDX_TILES * KT * 4 + (kBarBytes + 127) / 128 * 128;  // ~101 KB
+    1024 + STAGES * STAGE_BYTES + CBUF_BYTES + NPROD * IDX_TILES * KT * 4 + (kBarBytes + 127) / 128 * 128;  // ~103 KB
 
 template <typename X>
 tcaspmm_status upload_vec(Shard *sh, X **dst, const std::vector<X> &v, const char *what)
