@@ -39,7 +39,11 @@ typedef enum tcaspmm_status {
 typedef enum tcaspmm_dtype {
     TCASPMM_F32 = 0,
     TCASPMM_F16 = 1,
-    TCASPMM_BF16 = 2
+    TCASPMM_BF16 = 2,
+    /* fp32 storage (B and A's values as fp32); tensor-core windows multiply in
+     * TF32 (tcgen05 kind::tf32, 10-bit mantissa, fp32 accumulate), the CUDA-core
+     * residue stays fp32.  Opt-in: TCASPMM_F32 never uses the tensor cores. */
+    TCASPMM_TF32 = 3
 } tcaspmm_dtype;
 
 /* Replaces mat_format {dense, csr, coo} (src/mat_format.cuh:10-15). */

@@ -50,6 +50,7 @@ class dtype(enum.IntEnum):
     f32 = 0
     f16 = 1
     bf16 = 2
+    tf32 = 3  # fp32 storage; tensor-core windows multiply in TF32
 
 
 class mat_format(enum.IntEnum):
@@ -62,7 +63,7 @@ class mat_format(enum.IntEnum):
 
 MATTYPE_STRING = ("DENSE", "CSR", "COO")
 
-_NP_OF = {dtype.f32: np.float32, dtype.f16: np.float16, dtype.bf16: np.uint16}
+_NP_OF = {dtype.f32: np.float32, dtype.f16: np.float16, dtype.bf16: np.uint16, dtype.tf32: np.float32}
 
 
 def as_dtype(d) -> dtype:
@@ -70,7 +71,7 @@ def as_dtype(d) -> dtype:
         return d
     if isinstance(d, str):
         return {"f32": dtype.f32, "fp32": dtype.f32, "float32": dtype.f32, "f16": dtype.f16, "fp16": dtype.f16,
-                "float16": dtype.f16, "half": dtype.f16, "bf16": dtype.bf16, "bfloat16": dtype.bf16}[d]
+                "float16": dtype.f16, "half": dtype.f16, "bf16": dtype.bf16, "bfloat16": dtype.bf16, "tf32": dtype.tf32}[d]
     try:
         import torch
 

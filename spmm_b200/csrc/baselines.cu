@@ -27,7 +27,7 @@ tcaspmm_status bfail(tcaspmm_status s, const char *what, int code)
 
 cudaDataType_t cuda_type(tcaspmm_dtype dt)
 {
-    return dt == TCASPMM_F32 ? CUDA_R_32F : dt == TCASPMM_F16 ? CUDA_R_16F : CUDA_R_16BF;
+    return (dt == TCASPMM_F32 || dt == TCASPMM_TF32) ? CUDA_R_32F : dt == TCASPMM_F16 ? CUDA_R_16F : CUDA_R_16BF;
 }
 
 // L2 flush between timed calls (set by tcaspmm_baselines_set_flush): the same
@@ -149,7 +149,7 @@ extern "C" tcaspmm_status tcaspmm_cusparse_blocked_ell(const tcaspmm_csr *A, int
                                                       float *dC, int64_t ldc, int64_t N, tcaspmm_dtype dt, int warmup,
                                                       int iters, void *stream, double *ms_per_iter, int64_t *ell_bytes)
 {
-    if (!A || !ms_per_iter || block < 1 || dt == TCASPMM_F32) return TCASPMM_ERR_INVALID_ARG;
+    if (!A || !ms_per_iter || block < 1 || dt == TCASPMM_F32 || dt == TCASPMM_TF32) return TCASPMM_ERR_INVALID_ARG;
     tcaspmm_status s = tcaspmm_csr_validate(A);
     if (s != TCASPMM_OK) return s;
     const int64_t M = A->nrow, K = A->ncol;

@@ -66,7 +66,7 @@ tcaspmm_status tcaspmm_gen_dense(int64_t rows, int64_t cols, uint64_t seed, tcas
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < n; i++) {
         const float x = (float)rng_normal(seed, S_DENSE, (uint64_t)i);
-        if (dt == TCASPMM_F32)
+        if (dtype_fp32(dt))
             ((float *)out)[i] = x;
         else if (dt == TCASPMM_F16)
             ((uint16_t *)out)[i] = float_to_half_bits(x);

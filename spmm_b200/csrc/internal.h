@@ -15,8 +15,12 @@ tcaspmm_status fail(tcaspmm_status s, const char *fmt, ...);
 void clear_error();
 
 // ---- dtype helpers ----
-inline int dtype_size(tcaspmm_dtype dt) { return dt == TCASPMM_F32 ? 4 : 2; }
-inline bool dtype_valid(int dt) { return dt == TCASPMM_F32 || dt == TCASPMM_F16 || dt == TCASPMM_BF16; }
+inline bool dtype_fp32(tcaspmm_dtype dt) { return dt == TCASPMM_F32 || dt == TCASPMM_TF32; }  // fp32 storage
+inline int dtype_size(tcaspmm_dtype dt) { return dtype_fp32(dt) ? 4 : 2; }
+inline bool dtype_valid(int dt)
+{
+    return dt == TCASPMM_F32 || dt == TCASPMM_F16 || dt == TCASPMM_BF16 || dt == TCASPMM_TF32;
+}
 uint16_t float_to_half_bits(float f);
 uint16_t float_to_bf16_bits(float f);
 float half_bits_to_float(uint16_t h);

@@ -301,7 +301,7 @@ extern "C" tcaspmm_status tcaspmm_spmm_csr_noalloc(const int32_t *d_row_ptr, con
     const int elem = dtype_size(dt);
     const bool vec = ((uintptr_t)dB % 16 == 0) && ((ldb * elem) % 16 == 0) && ((uintptr_t)dC % 16 == 0) &&
                      (ldc % 4 == 0) && (N % (16 / elem) == 0);
-    if (dt == TCASPMM_F32)
+    if (dtype_fp32(dt))  // TF32 plans have fp32 storage; this path computes in fp32
         launch_t<float>(vec, p, st);
     else if (dt == TCASPMM_F16)
         launch_t<__half>(vec, p, st);

@@ -122,7 +122,7 @@ tcaspmm_status build_shard(const tcaspmm_csr &Afull, tcaspmm_dtype dt, int devic
             ones.assign((size_t)A.nnz, 1.0f);
             v = ones.data();
         }
-        if (dt == TCASPMM_F32) {
+        if (dtype_fp32(dt)) {
             float *d = nullptr;
             if ((s = upload(*sh, &d, v, (size_t)A.nnz, "values")) != TCASPMM_OK) return s;
             sh->val = d;

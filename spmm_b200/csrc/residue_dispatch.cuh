@@ -45,7 +45,7 @@ void launch_res_t(bool vec, int G, const ResidueParams &p, int total_warps, cuda
 template <bool EPI>
 void launch_res_dt(tcaspmm_dtype dt, bool vec, int G, const ResidueParams &p, int total_warps, cudaStream_t st)
 {
-    if (dt == TCASPMM_F32)
+    if (dt == TCASPMM_F32 || dt == TCASPMM_TF32)
         launch_res_t<float, EPI>(vec, G, p, total_warps, st);
     else if (dt == TCASPMM_F16)
         launch_res_t<__half, EPI>(vec, G, p, total_warps, st);

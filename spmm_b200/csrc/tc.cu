@@ -55,29 +55,54 @@ namespace tca {
 namespace {
 
 constexpr int R = 32;            // window rows = MMA N
-constexpr int KT = 16;           // condensed columns per tile = MMA K (16-bit inputs)
+constexpr int KT = 16;           // condensed columns per tile
 constexpr int MB = 128;          // output columns per unit = MMA M
-constexpr int TPS = 4;           // tiles per pipeline stage: one stage = K of 64
-constexpr int STAGES = 4;  // 16 tiles in flight per CTA, ~82 KB: two CTAs per SM
-constexpr int IDX_TILES = 32;    // tile column indices staged per refill (a multiple of TPS)
-constexpr int TILE_PANEL_BYTES = MB * KT * 2;          // 4 KB of B panel per tile
-constexpr int PANEL_BYTES = TPS * TILE_PANEL_BYTES;    // 16 KB per stage
-constexpr int HALF_BYTES = PANEL_BYTES / 2;            // one 64-column half: 8 k-groups of 1 KB atoms
-constexpr int VAL_BYTES = R * KT * 2;                  // 1 KB of values per tile
-constexpr int STAGE_BYTES = PANEL_BYTES + TPS * VAL_BYTES;
+constexpr int STAGES = 4;        // pipeline stages of 20 KB
+constexpr int IDX_TILES = 32;    // tile column indices staged per refill (a multiple of every TPS)
+constexpr int PANEL_BYTES = 16384;                     // B panel per stage (any element type)
+constexpr int STAGE_BYTES = PANEL_BYTES + 4096;        // + the stage's value tiles
+
+// Element-type geometry.  FMT 0 = fp16, 1 = bf16 (kind::f16, 2-byte elements),
+// 2 = tf32 (kind::tf32, fp32 storage).  A 128-byte swizzle atom row holds CPB
+// columns, so the 128-column panel is NPC column pieces; a stage holds TPS tiles
+// (SROWS B rows), so every stage is 16 KB of panel + 4 KB of values.  Within a
+// piece, B row k of the stage sits in atom k / 8 (1 KB apart), so tile j starts
+// 2 KB into every piece whatever the type.
+template <int FMT> struct Geo {
+    static constexpr int ES = FMT == 2 ? 4 : 2;      // element bytes
+    static constexpr int TPS = 8 / ES;               // tiles per stage: 4 or 2
+    static constexpr int SROWS = TPS * KT;           // B rows per stage: 64 or 32
+    static constexpr int CPB = 128 / ES;             // columns per piece: 64 or 32
+    static constexpr int NPC = MB / CPB;             // pieces per panel: 2 or 4
+    static constexpr int PIECE = SROWS / 8 * 1024;   // bytes of one piece in a stage: 8 or 4 KB
+    static constexpr int TILE_PANEL = MB * KT * ES;  // panel bytes per tile: 4 or 8 KB
+    static constexpr int TILE_VAL = R * KT * ES;     // value bytes per tile: 1 or 2 KB
+    static constexpr int KSTEP = 32 / ES;            // K of one MMA: 16 or 8
+    static constexpr int KCH = KT * ES / 16;         // 16-byte k chunks per value-tile row: 2 or 4
+    // Panel swizzle, as the smem-descriptor layout type: 128-byte swizzle of
+    // 16-byte chunks (2) for 16-bit types; MN-major tf32 operands take the
+    // 128-byte swizzle of 32-byte chunks (1), which TMA writes with
+    // CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B.
+    static constexpr uint32_t LAYOUT = FMT == 2 ? 1u : 2u;
+    // Stride between the k-row groups the MMA walks through (SBO): 8-row atoms
+    // of 1 KB for 16-bit types; 4-row groups (512 B) for tf32 (measured: with
+    // 1 KB, k rows 4-7 of each group were read from rows 8-11).
+    static constexpr uint32_t KGROUP = FMT == 2 ? 512u : 1024u;
+    static_assert(TPS * TILE_PANEL == PANEL_BYTES && TPS * TILE_VAL == STAGE_BYTES - PANEL_BYTES, "stage size");
+    static_assert(IDX_TILES % TPS == 0, "stages must not straddle index refills");
+};
 constexpr int TMEM_COLS = 2 * R;  // two accumulators
 constexpr int NPROD = 2;  // producer warps, taking stages round-robin
 constexpr int NUM_THREADS = 160 + 32 * NPROD;
 constexpr int CBUF_BYTES = 4 * 32 * 32 * 4;  // C staging: a 32 x 32 fp32 tile per epilogue warp
 constexpr int EPI_THREADS = 128;
 constexpr unsigned long long WAIT_CYCLES = 4ull << 30;  // ~2 s at 2 GHz: no legitimate wait comes close
-static_assert(IDX_TILES % TPS == 0, "stages must not straddle index refills");
 
 struct TcParams {
     const int4 *windows;     // {first row, first tile, tiles, rows}, by decreasing tile count
     const int32_t *dense_c0; // per window: first column when its columns are one consecutive run, else -1
     const int32_t *tile_cols;
-    const uint16_t *tile_vals;
+    const uint8_t *tile_vals;  // per tile: the value tile's shared-memory image
     const void *B;
     long long ldb;
     void *C;                 // fp32, or 16-bit with the epilogue
@@ -185,7 +210,7 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
 {
     // tcgen05 shared-memory descriptor: start address, leading / stride byte
     // offsets (all >> 4), version 1 (bits 46-47), layout type (bits 61-63:
-    // 0 no swizzle, 2 128-byte swizzle).
+    // 0 no swizzle, 1 128-byte swizzle of 32-byte chunks, 2 128-byte swizzle).
     return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
            ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
 }
@@ -229,25 +254,34 @@ struct BMaps {
     CUtensorMap box64;
 };
 
-template <bool BF16>
+template <int FMT>
 __device__ __forceinline__ constexpr uint32_t instr_desc()
 {
-    // kind::f16 instruction descriptor: D fp32 (bits 4-5 = 1), A/B format
-    // (bits 7-9, 10-12: 0 f16, 1 bf16), A MN-major (bit 15), B K-major (bit 16 = 0),
-    // N >> 3 (bits 17-22), M >> 4 (bits 24-28).
-    return (1u << 4) | ((BF16 ? 1u : 0u) << 7) | ((BF16 ? 1u : 0u) << 10) | (1u << 15) | ((uint32_t)(R >> 3) << 17) |
+    // kind::f16 / kind::tf32 instruction descriptor: D fp32 (bits 4-5 = 1), A/B
+    // format (bits 7-9, 10-12: 0 f16, 1 bf16, 2 tf32), A MN-major (bit 15), B
+    // K-major (bit 16 = 0), N >> 3 (bits 17-22), M >> 4 (bits 24-28).
+    return (1u << 4) | ((uint32_t)FMT << 7) | ((uint32_t)FMT << 10) | (1u << 15) | ((uint32_t)(R >> 3) << 17) |
            ((uint32_t)(MB >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                        uint32_t accumulate)
+template <int FMT>
+__device__ __forceinline__ void mma_issue(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate)
 {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
+    if constexpr (FMT == 2)
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+            : "memory");
+    else
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+            : "memory");
 }
 
 __device__ __forceinline__ void mma_commit(uint32_t bar)
@@ -276,7 +310,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <bool BF16>
+template <int FMT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_kernel(const TcParams p, const __grid_constant__ BMaps maps, const __grid_constant__ CUtensorMap cmap)
 {
@@ -294,6 +328,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t *tmem_holder = (uint32_t *)(bars + 2 * STAGES + 5);
     volatile int *abort_flag = (volatile int *)(tmem_holder + 1);
 
+    using G = Geo<FMT>;
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
@@ -356,7 +391,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int4 w = first ? w_first : p.windows[win];
             const int c0 = first ? c_first : p.dense_c0[win];
             const int n0 = (u % p.nfb) * MB;
-            const int nst = (w.z + TPS - 1) / TPS;  // stages of this unit (w.z >= 1)
+            const int nst = (w.z + G::TPS - 1) / G::TPS;  // stages of this unit (w.z >= 1)
             const int rot = win % nst;
             if (c0 >= 0) {
                 // One consecutive run of columns c0, c0 + 1, ...: tile t covers B
@@ -364,9 +399,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 // past K are zero-filled by TMA), so no indices are loaded.
                 for (int k = 0; ok && k < nst; ++k, ++g) {
                     if ((int)(g % NPROD) != pw) continue;
-                    const int t = stage_at(k, rot, nst) * TPS;
+                    const int t = stage_at(k, rot, nst) * G::TPS;
                     const int s = g % STAGES;
-                    const int n = min(TPS, w.z - t);
+                    const int n = min(G::TPS, w.z - t);
                     ok = __all_sync(0xffffffffu, wait_bounded(smem_u32(&empty[s]), ((g / STAGES) & 1) ^ 1,
                                                               abort_flag, p.err, 1, p.wait_cycles));
                     if (!ok) break;
@@ -374,26 +409,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         const uint32_t fb = smem_u32(&full[s]);
                         const uint32_t panel = smem_u32(smem + s * STAGE_BYTES);
                         const int y = c0 + t * KT;
-                        mbar_expect_tx(fb, (uint32_t)n * (TILE_PANEL_BYTES + VAL_BYTES));
-                        if (n == TPS) {
-                            tma_box(panel, tm_64, n0, y, fb);
-                            tma_box(panel + HALF_BYTES, tm_64, n0 + 64, y, fb);
+                        mbar_expect_tx(fb, (uint32_t)n * (G::TILE_PANEL + G::TILE_VAL));
+                        if (n == G::TPS) {
+#pragma unroll
+                            for (int c = 0; c < G::NPC; ++c) tma_box(panel + c * G::PIECE, tm_64, n0 + c * G::CPB, y, fb);
                         } else {
-                            for (int j = 0; j < n; ++j) {
-                                const uint32_t tp = panel + j * TILE_PANEL_BYTES / 2;
-                                tma_box(tp, tm_16, n0, y + j * KT, fb);
-                                tma_box(tp + HALF_BYTES, tm_16, n0 + 64, y + j * KT, fb);
-                            }
+                            for (int j = 0; j < n; ++j)
+#pragma unroll
+                                for (int c = 0; c < G::NPC; ++c)
+                                    tma_box(panel + c * G::PIECE + j * 2048, tm_16, n0 + c * G::CPB, y + j * KT, fb);
                         }
-                        bulk_copy(panel + PANEL_BYTES, p.tile_vals + ((long long)w.y + t) * (R * KT),
-                                  (uint32_t)n * VAL_BYTES, fb);
+                        bulk_copy(panel + PANEL_BYTES, p.tile_vals + ((long long)w.y + t) * G::TILE_VAL,
+                                  (uint32_t)n * G::TILE_VAL, fb);
                     }
                 }
                 continue;
             }
             int chunk = -1;  // IDX_TILES-tile chunk whose indices are staged
             for (int k = 0; ok && k < nst; ++k, ++g) {
-                const int t = stage_at(k, rot, nst) * TPS;  // first tile of the stage
+                const int t = stage_at(k, rot, nst) * G::TPS;  // first tile of the stage
                 if (t / IDX_TILES != chunk) {
                     chunk = t / IDX_TILES;
                     const int t0 = chunk * IDX_TILES, nt = min(IDX_TILES, w.z - t0);
@@ -404,7 +438,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 if ((int)(g % NPROD) != pw) continue;
                 const int s = g % STAGES;
-                const int n = min(TPS, w.z - t);  // tiles in this stage
+                const int n = min(G::TPS, w.z - t);  // tiles in this stage
                 ok = __all_sync(0xffffffffu, wait_bounded(smem_u32(&empty[s]), ((g / STAGES) & 1) ^ 1, abort_flag,
                                                           p.err, 1, p.wait_cycles));
                 if (!ok) break;
@@ -412,34 +446,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint32_t fb = smem_u32(&full[s]);
                     const uint32_t panel = smem_u32(smem + s * STAGE_BYTES);
                     const int32_t *ix = myidx + (t - chunk * IDX_TILES) * KT;
-                    mbar_expect_tx(fb, (uint32_t)n * (TILE_PANEL_BYTES + VAL_BYTES));
+                    mbar_expect_tx(fb, (uint32_t)n * (G::TILE_PANEL + G::TILE_VAL));
                     // A window's columns ascend, distinct except the padding of
                     // its last tile, which repeats the last column.  So m
                     // indices whose span is m - 1 and whose last two differ
                     // are m consecutive B rows.
-                    if (n == TPS && ix[TPS * KT - 1] - ix[0] == TPS * KT - 1 && ix[TPS * KT - 2] != ix[TPS * KT - 1]) {
-                        tma_box(panel, tm_64, n0, ix[0], fb);
-                        tma_box(panel + HALF_BYTES, tm_64, n0 + 64, ix[0], fb);
+                    if (n == G::TPS && ix[G::SROWS - 1] - ix[0] == G::SROWS - 1 && ix[G::SROWS - 2] != ix[G::SROWS - 1]) {
+#pragma unroll
+                        for (int c = 0; c < G::NPC; ++c) tma_box(panel + c * G::PIECE, tm_64, n0 + c * G::CPB, ix[0], fb);
                     } else {
                         for (int j = 0; j < n; ++j) {
                             const int32_t *jx = ix + j * KT;
-                            const uint32_t tp = panel + j * TILE_PANEL_BYTES / 2;
+                            const uint32_t tp = panel + j * 2048;
                             if (jx[KT - 1] - jx[0] == KT - 1 && jx[KT - 2] != jx[KT - 1]) {
-                                tma_box(tp, tm_16, n0, jx[0], fb);
-                                tma_box(tp + HALF_BYTES, tm_16, n0 + 64, jx[0], fb);
+#pragma unroll
+                                for (int c = 0; c < G::NPC; ++c)
+                                    tma_box(tp + c * G::PIECE, tm_16, n0 + c * G::CPB, jx[0], fb);
                             } else {
 #pragma unroll
-                                for (int c = 0; c < 2; ++c)
+                                for (int c = 0; c < G::NPC; ++c)
 #pragma unroll
                                     for (int q = 0; q < 4; ++q)
-                                        tma_gather4(tp + c * HALF_BYTES + (q >> 1) * 1024 + (q & 1) * 512, tm_g,
-                                                    n0 + 64 * c, jx[4 * q], jx[4 * q + 1], jx[4 * q + 2],
+                                        tma_gather4(tp + c * G::PIECE + (q >> 1) * 1024 + (q & 1) * 512, tm_g,
+                                                    n0 + c * G::CPB, jx[4 * q], jx[4 * q + 1], jx[4 * q + 2],
                                                     jx[4 * q + 3], fb);
                             }
                         }
                     }
-                    bulk_copy(panel + PANEL_BYTES, p.tile_vals + ((long long)w.y + t) * (R * KT),
-                              (uint32_t)n * VAL_BYTES, fb);
+                    bulk_copy(panel + PANEL_BYTES, p.tile_vals + ((long long)w.y + t) * G::TILE_VAL,
+                              (uint32_t)n * G::TILE_VAL, fb);
                 }
             }
         }
@@ -456,7 +491,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     } else if (warp == 4) {
         // ------------------------------ MMA issuer -----------------------------
         if (lane == 0) {
-            constexpr uint32_t idesc = instr_desc<BF16>();
+            constexpr uint32_t idesc = instr_desc<FMT>();
             uint32_t g = 0, i = 0;
             bool ok = true;
             for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x, ++i) {
@@ -467,12 +502,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 const uint32_t dcol = tmem + a * R;
                 // Stages in the producer's order: TPS tiles each, starting at
                 // the window's stage offset.
-                const int nst = (w.z + TPS - 1) / TPS;
+                const int nst = (w.z + G::TPS - 1) / G::TPS;
                 const int rot = (u / p.nfb) % nst;
                 for (int k = 0; k < nst; ++k, ++g) {
                     const int s = g % STAGES;
-                    const int t = stage_at(k, rot, nst) * TPS;
-                    const int n = min(TPS, w.z - t);
+                    const int t = stage_at(k, rot, nst) * G::TPS;
+                    const int n = min(G::TPS, w.z - t);
                     if (!wait_bounded(smem_u32(&full[s]), (g / STAGES) & 1, abort_flag, p.err, 2, p.wait_cycles)) {
                         ok = false;
                         break;
@@ -480,10 +515,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     tc_fence_after();
                     const uint32_t panel = smem_u32(smem + s * STAGE_BYTES);
                     for (int j = 0; j < n; ++j) {
-                        // A: MN-major, 128-byte swizzle; B: K-major, no swizzle.
-                        const uint64_t adesc = smem_desc(panel + j * 2048, HALF_BYTES, 1024, 2);
-                        const uint64_t bdesc = smem_desc(panel + PANEL_BYTES + j * VAL_BYTES, 128, 256, 0);
-                        mma_f16(dcol, adesc, bdesc, idesc, (k | j) != 0 ? 1u : 0u);
+#pragma unroll
+                        for (int h = 0; h < KT / G::KSTEP; ++h) {
+                            // A: MN-major, 128-byte swizzle, pieces LBO apart, 8-row
+                            // atoms SBO apart; B: K-major, no swizzle, 16-byte k chunks
+                            // LBO apart, 8-row groups SBO apart.
+                            const uint64_t adesc =
+                                smem_desc(panel + j * 2048 + h * (G::KSTEP / 8) * 1024, G::PIECE, G::KGROUP, G::LAYOUT);
+                            const uint64_t bdesc = smem_desc(
+                                panel + PANEL_BYTES + j * G::TILE_VAL + h * (G::KSTEP * G::ES / 16) * 128, 128,
+                                G::KCH * 128, 0);
+                            mma_issue<FMT>(dcol, adesc, bdesc, idesc, (k | j | h) != 0 ? 1u : 0u);
+                        }
                     }
                     mma_commit(smem_u32(&empty[s]));
                 }
@@ -614,42 +657,54 @@ EncodeTiledFn encode_fn()
     return fn;
 }
 
+// The kernel's element format for a plan dtype: 0 fp16, 1 bf16, 2 tf32.
+int fmt_of(tcaspmm_dtype dt) { return dt == TCASPMM_BF16 ? 1 : dt == TCASPMM_TF32 ? 2 : 0; }
+
 // Tensor maps over a B block of ncols columns x K rows (x = column, zero fill
-// beyond ncols; y = B row), 128-byte swizzle, boxes 64 x 1, 64 x 16, 64 x 64.
+// beyond ncols; y = B row), 128-byte swizzle, boxes of one 128-byte piece (64
+// 16-bit or 32 fp32 columns) x 1, 16 and one stage of rows (64 or 32).
 tcaspmm_status encode_b_maps(tcaspmm_dtype dt, const void *dB, int64_t ncols, int64_t K, int64_t ldb, BMaps *m)
 {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return fail(TCASPMM_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const int fmt = fmt_of(dt);
+    const int es = fmt == 2 ? 4 : 2;
+    const cuuint32_t cpb = 128 / es, srows = fmt == 2 ? Geo<2>::SROWS : Geo<0>::SROWS;
     const cuuint64_t dims[2] = {(cuuint64_t)ncols, (cuuint64_t)K};
-    const cuuint64_t strides[1] = {(cuuint64_t)ldb * 2};
+    const cuuint64_t strides[1] = {(cuuint64_t)(ldb * es)};
     const cuuint32_t estr[2] = {1, 1};
-    const CUtensorMapDataType ty = dt == TCASPMM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    // Boxes of 16 / 64 rows are used only where that many consecutive B rows
-    // exist, so on a B of fewer rows they are clipped to K (never issued).
-    const cuuint32_t k16 = (cuuint32_t)std::min<int64_t>(KT, K), k64 = (cuuint32_t)std::min<int64_t>(TPS * KT, K);
-    const cuuint32_t boxes[3][2] = {{64, 1}, {64, k16}, {64, k64}};
+    const CUtensorMapDataType ty = fmt == 1   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                   : fmt == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    // Boxes of 16 / one stage of rows are used only where that many consecutive
+    // B rows exist, so on a B of fewer rows they are clipped to K (never issued).
+    const cuuint32_t k16 = (cuuint32_t)std::min<int64_t>(KT, K), ks = (cuuint32_t)std::min<int64_t>(srows, K);
+    const cuuint32_t boxes[3][2] = {{cpb, 1}, {cpb, k16}, {cpb, ks}};
     CUtensorMap *maps[3] = {&m->gather, &m->box16, &m->box64};
     CUresult r = CUDA_SUCCESS;
+    const CUtensorMapSwizzle sw = fmt == 2 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
     for (int i = 0; i < 3 && r == CUDA_SUCCESS; ++i)
-        r = fn(maps[i], ty, 2, const_cast<void *>(dB), dims, strides, boxes[i], estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        r = fn(maps[i], ty, 2, const_cast<void *>(dB), dims, strides, boxes[i], estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? TCASPMM_OK : fail(TCASPMM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
 }
 
 static_assert(sizeof(BMaps) <= sizeof(Shard::maps) && sizeof(CUtensorMap) <= sizeof(Shard::cmap), "tensor-map storage in Shard");
 
-template <bool BF16>
+template <int FMT>
 cudaError_t smem_optin()
 {
-    return cudaFuncSetAttribute(tc_kernel<BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    return cudaFuncSetAttribute(tc_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
 }
 
-void launch_kernel(bool bf16, int grid, const TcParams &p, const BMaps &maps, const CUtensorMap &cmap, cudaStream_t st)
+void launch_kernel(int fmt, int grid, const TcParams &p, const BMaps &maps, const CUtensorMap &cmap, cudaStream_t st)
 {
-    if (bf16)
-        tc_kernel<true><<<grid, NUM_THREADS, kSmemBytes, st>>>(p, maps, cmap);
+    if (fmt == 1)
+        tc_kernel<1><<<grid, NUM_THREADS, kSmemBytes, st>>>(p, maps, cmap);
+    else if (fmt == 2)
+        tc_kernel<2><<<grid, NUM_THREADS, kSmemBytes, st>>>(p, maps, cmap);
     else
-        tc_kernel<false><<<grid, NUM_THREADS, kSmemBytes, st>>>(p, maps, cmap);
+        tc_kernel<0><<<grid, NUM_THREADS, kSmemBytes, st>>>(p, maps, cmap);
 }
 
 // Tensor map over a C block of ncols x rows elements of the output type (ldc
@@ -690,21 +745,30 @@ tcaspmm_status tc_upload(const tcaspmm_csr &, tcaspmm_dtype dt, Shard *sh)
     // (Sorted on the host, so the kernel reads a unit's window with one load.)
     std::vector<Int4> windows(T.windows);
     std::stable_sort(windows.begin(), windows.end(), [](const Int4 &a, const Int4 &b) { return a.z > b.z; });
-    // Value tiles -> shared-memory image (K-major, no swizzle, LBO 128 B, SBO 256 B).
+    // Value tiles -> shared-memory image (K-major, no swizzle): core matrices of
+    // 8 rows x 16 bytes, 16-byte k chunks 128 B apart (LBO), 8-row groups
+    // kch * 128 B apart (SBO); fp16 / bf16 bits, or fp32 bits for tf32.
+    const int es = dtype_size(dt), kch = KT * es / 16, tile_bytes = R * KT * es;
     const size_t ntiles = T.tile_cols.size() / KT;
-    std::vector<uint16_t> img(ntiles * R * KT);
+    std::vector<uint8_t> img(ntiles * tile_bytes);
     for (size_t t = 0; t < ntiles; t++)
         for (int n = 0; n < R; n++)
             for (int k = 0; k < KT; k++) {
                 const float v = T.tile_vals[(t * R + n) * KT + k];
-                img[t * R * KT + (n / 8) * 128 + (k / 8) * 64 + (n % 8) * 8 + (k % 8)] =
-                    dt == TCASPMM_BF16 ? float_to_bf16_bits(v) : float_to_half_bits(v);
+                uint8_t *dst = img.data() + t * tile_bytes + (n / 8) * (kch * 128) + (k * es / 16) * 128 +
+                               (n % 8) * 16 + (k * es) % 16;
+                if (es == 4) {
+                    std::memcpy(dst, &v, 4);
+                } else {
+                    const uint16_t h = dt == TCASPMM_BF16 ? float_to_bf16_bits(v) : float_to_half_bits(v);
+                    std::memcpy(dst, &h, 2);
+                }
             }
     // Windows whose columns are one consecutive run (padding repeats the last
     // column) need no index loads: their tiles are boxes of consecutive B rows.
     // Only when K >= 64, so that the 64- and 16-row boxes are never clipped.
     std::vector<int32_t> dense(windows.size(), -1);
-    for (size_t i = 0; i < windows.size() && sh->K >= TPS * KT; i++) {
+    for (size_t i = 0; i < windows.size() && sh->K >= 64; i++) {
         const int32_t *c = T.tile_cols.data() + (size_t)windows[i].y * KT;
         const int64_t n = (int64_t)windows[i].z * KT;
         bool ok = true;
@@ -722,17 +786,18 @@ tcaspmm_status tc_upload(const tcaspmm_csr &, tcaspmm_dtype dt, Shard *sh)
     if ((s = upload_vec(sh, &sh->tc_windows, windows, "tc windows")) != TCASPMM_OK) return s;
     if ((s = upload_vec(sh, &sh->tc_dense, dense, "tc dense runs")) != TCASPMM_OK) return s;
     if ((s = upload_vec(sh, &sh->tc_cols, T.tile_cols, "tc columns")) != TCASPMM_OK) return s;
-    if ((s = upload_vec(sh, (uint16_t **)&sh->tc_vals, img, "tc values")) != TCASPMM_OK) return s;
+    if ((s = upload_vec(sh, (uint8_t **)&sh->tc_vals, img, "tc values")) != TCASPMM_OK) return s;
     if ((s = upload_vec(sh, &sh->tc_fallback, fb, "tc fallback ranges")) != TCASPMM_OK) return s;
     int nsm = 148;
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, sh->device);
     sh->num_sms = nsm;
     // More than 48 KB of dynamic shared memory needs the opt-in, per device.
-    cudaError_t e = smem_optin<false>();
-    if (e == cudaSuccess) e = smem_optin<true>();
+    cudaError_t e = smem_optin<0>();
+    if (e == cudaSuccess) e = smem_optin<1>();
+    if (e == cudaSuccess) e = smem_optin<2>();
     int per_sm = 0;
     if (e == cudaSuccess)
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tc_kernel<false>, NUM_THREADS, kSmemBytes);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tc_kernel<0>, NUM_THREADS, kSmemBytes);
     sh->tc_ctas_per_sm = std::max(1, per_sm);
     return e == cudaSuccess ? TCASPMM_OK : cuda_fail(e, "tc kernel shared-memory opt-in");
 }
@@ -741,14 +806,14 @@ tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int6
                          const Epilogue *ep, cudaStream_t st)
 {
     if (sh.n_windows == 0 || sh.ncols == 0) return TCASPMM_OK;
-    const bool aligned = ((uintptr_t)dB % 16 == 0) && ((ldb * 2) % 16 == 0) && (sh.ncols % 8 == 0);
+    const bool aligned = ((uintptr_t)dB % 16 == 0) && ((ldb * dtype_size(dt)) % 16 == 0) && (sh.ncols % 8 == 0);
     if (!aligned)  // CUDA-core fallback over the tc rows: whole rows, no segments
         return launch_residue(sh, dt, dB, ldb, dC, ldc, ep, st, sh.tc_fallback, sh.n_windows);
     TcParams p;
     p.windows = (const int4 *)sh.tc_windows;
     p.dense_c0 = sh.tc_dense;
     p.tile_cols = sh.tc_cols;
-    p.tile_vals = (const uint16_t *)sh.tc_vals;
+    p.tile_vals = (const uint8_t *)sh.tc_vals;
     p.B = dB;
     p.ldb = ldb;
     p.C = dC;
@@ -785,7 +850,7 @@ tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int6
         sh.maps_ptr = dB;
         sh.maps_ldb = ldb;
     }
-    launch_kernel(dt == TCASPMM_BF16, grid, p, *(const BMaps *)sh.maps, *(const CUtensorMap *)sh.cmap, st);
+    launch_kernel(fmt_of(dt), grid, p, *(const BMaps *)sh.maps, *(const CUtensorMap *)sh.cmap, st);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TCASPMM_OK : cuda_fail(e, "tc kernel launch");
 }
@@ -819,7 +884,7 @@ extern "C" tcaspmm_status tcaspmm_selftest_tc_timeout(int device, unsigned long 
     alloc(&d_dense, sizeof(no_run));
     alloc(&d_cols, cols.size() * 4);
     alloc(&d_vals, vals.size() * 2);
-    alloc(&d_b, TPS * KT * MB * 2);
+    alloc(&d_b, Geo<0>::SROWS * MB * 2);
     alloc(&d_c, R * MB * 4);
     alloc((void **)&d_err, sizeof(int));
     BMaps maps;
@@ -828,16 +893,16 @@ extern "C" tcaspmm_status tcaspmm_selftest_tc_timeout(int device, unsigned long 
         cudaMemcpy(d_dense, &no_run, sizeof(no_run), cudaMemcpyHostToDevice);
         cudaMemcpy(d_cols, cols.data(), cols.size() * 4, cudaMemcpyHostToDevice);
         cudaMemcpy(d_vals, vals.data(), vals.size() * 2, cudaMemcpyHostToDevice);
-        cudaMemset(d_b, 0, TPS * KT * MB * 2);
+        cudaMemset(d_b, 0, Geo<0>::SROWS * MB * 2);
         cudaMemset(d_err, 0, sizeof(int));
-        st = encode_b_maps(TCASPMM_F16, d_b, MB, TPS * KT, MB, &maps);
+        st = encode_b_maps(TCASPMM_F16, d_b, MB, Geo<0>::SROWS, MB, &maps);
     }
     if (st == TCASPMM_OK) {
         TcParams p;
         p.windows = (const int4 *)d_win;
         p.dense_c0 = (const int32_t *)d_dense;
         p.tile_cols = (const int32_t *)d_cols;
-        p.tile_vals = (const uint16_t *)d_vals;
+        p.tile_vals = (const uint8_t *)d_vals;
         p.B = d_b;
         p.ldb = MB;
         p.C = (float *)d_c;
@@ -851,9 +916,9 @@ extern "C" tcaspmm_status tcaspmm_selftest_tc_timeout(int device, unsigned long 
         p.has_ep = 0;
         p.ep = EpiParams{nullptr, nullptr, 0, 0};
         p.tma_store = 0;
-        e = smem_optin<false>();
+        e = smem_optin<0>();
         if (e == cudaSuccess) {
-            launch_kernel(false, 1, p, maps, CUtensorMap{}, 0);
+            launch_kernel(0, 1, p, maps, CUtensorMap{}, 0);
             e = cudaGetLastError();
         }
         if (e == cudaSuccess) e = cudaDeviceSynchronize();

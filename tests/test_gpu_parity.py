@@ -18,7 +18,7 @@ TOL_TC = 5e-3
 
 
 def _torch_dt(dt):
-    return {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[dt]
+    return {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16, "tf32": torch.float32}[dt]
 
 
 def _round(x: np.ndarray, dt: str) -> np.ndarray:
@@ -184,7 +184,7 @@ def test_multi_gpu_column_shards():
     assert oracle.rel_l2(out, reference(A, B, dt)) <= TOL_CORE
 
 
-@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("dt", ["f16", "bf16", "tf32"])
 @pytest.mark.parametrize("N", [256, 128, 64, 8, 200])
 def test_tensor_core_windows(dt, N):
     """C1 at 70% sparsity: every window is dense enough for the tcgen05 tiles."""
@@ -225,16 +225,25 @@ def test_tensor_core_integer_values_bit_exact():
     np.testing.assert_array_equal(out, reference(A, B, "f16").astype(np.float32))
 
 
+@pytest.mark.parametrize("dt", ["f16", "tf32"])
 @pytest.mark.parametrize("K", [12, 40, 64, 70])
-def test_tensor_core_windows_with_few_b_rows(K):
+def test_tensor_core_windows_with_few_b_rows(K, dt):
     """K below the 16- and 64-row TMA boxes: the boxes are clipped to K and only
     the forms that fit are issued (no index-free runs below K = 64)."""
     A = T.gen_uniform(256, K, 0.6, K)
     A = T.CSR(A.nrow, A.ncol, A.row_ptr, A.col, np.round(A.val * 4).astype(np.float32))
     B = np.round(T.gen_dense(K, 64, 3, "f32") * 4).astype(np.float32)
-    out, st = run(A, B, "f16")
+    out, st = run(A, B, dt)
     assert st["tc_windows"] > 0
-    np.testing.assert_array_equal(out, reference(A, B, "f16").astype(np.float32))
+    np.testing.assert_array_equal(out, reference(A, B, dt).astype(np.float32))
+
+
+def test_fp32_never_uses_tensor_cores_tf32_does():
+    """TCASPMM_F32 keeps the fp32 CUDA-core path (1e-5); TF32 is the opt-in tensor-core form (5e-3)."""
+    A = T.gen_uniform(1024, 512, 0.3, 5)
+    _, st32 = check(A, 128, "f32")
+    _, sttf = check(A, 128, "tf32")
+    assert st32["tc_windows"] == 0 and sttf["tc_windows"] == 32
 
 
 @pytest.mark.parametrize("dt", ["f32", "f16"])
@@ -319,7 +328,7 @@ def test_tensor_core_stage_shapes_bit_exact():
     ]
     A = _window_union_matrix(unions, K)
     B = np.round(T.gen_dense(K, 256, 5, "f32") * 4).astype(np.float32)
-    for dt in ("f16", "bf16"):
+    for dt in ("f16", "bf16", "tf32"):
         for N in (256, 136):
             out, st = run(A, B[:, :N], dt)
             assert st["tc_windows"] == len(unions) and st["tc_nnz"] == st["nnz"], st
