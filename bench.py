@@ -166,9 +166,12 @@ def run_reference(args, wl):
     if rank != 0:
         return 0
     desc, build, N, dt = wl
+    if args.dtype:
+        dt = args.dtype
+        desc += f" [dtype {dt}]"
     A = build(T)
     B = T.gen_dense(A.ncol, N, 1, "f32")
-    if dt != "f32":
+    if dt in ("f16", "bf16"):
         B = B.astype(np.float16).astype(np.float32)
     threads = host_threads()
     vals = A.values()
@@ -211,6 +214,8 @@ def main():
     ap.add_argument("--workload", default="gcn", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--dtype", default=None, choices=["f32", "tf32", "f16", "bf16"],
+                    help="override the workload's dtype (e.g. tf32: fp32 B through the TF32 tensor-core path)")
     ap.add_argument("--epilogue", action="store_true",
                     help="fused epilogue: C = relu(row_scale * (A B) + bias) stored as bf16")
     ap.add_argument("--gather", action="store_true",
@@ -242,8 +247,11 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
 
     desc, build, N, dt = wl
-    tdt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[dt]
-    elem = 4 if dt == "f32" else 2
+    if args.dtype:
+        dt = args.dtype
+        desc += f" [dtype {dt}]"
+    tdt = {"f32": torch.float32, "tf32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[dt]
+    elem = 4 if dt in ("f32", "tf32") else 2
     A = build(T)
     M, K, nnz = A.nrow, A.ncol, A.nnz
     Bfull = T.gen_dense(K, N, 1, dt)  # host, dt (bf16 as uint16 bits)
@@ -410,7 +418,7 @@ def main():
         ms_cusparse, cs_err = None, str(e)
     # Blocked-ELL (32 x 32 blocks) where A is small enough to be dense-ish (C1 / C2 shapes).
     bell = None
-    if dt != "f32" and M * K <= 1 << 26 and args.split == "columns" and ep is None:
+    if dt in ("f16", "bf16") and M * K <= 1 << 26 and args.split == "columns" and ep is None:
         try:
             Cb = torch.empty_like(Cd, dtype=torch.float32)
             bell_ms, _ = T.cusparse_blocked_ell(A, 32, Bd, Cb, dt, warmup=3, iters=max(5, min(args.steps, 50)),

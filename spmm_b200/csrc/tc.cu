@@ -8,23 +8,23 @@
 //
 // One unit = (window, block of 128 output columns).  Per unit the kernel
 // computes the transposed tile  C^T[128 x R] = Bpanel^T[128 x 16k] * V^T[16k x R]
-// with tcgen05.mma.kind::f16, M = 128 (output columns -> TMEM lanes),
-// N = R (window rows -> TMEM columns), K = 16 per tile, fp32 accumulation in
-// TMEM across the window's tiles.
+// with tcgen05.mma.kind::f16 (fp16 / bf16) or kind::tf32, M = 128 (output
+// columns -> TMEM lanes), N = R (window rows -> TMEM columns), fp32 accumulation
+// in TMEM across the window's tiles.
 //
 // Shared-memory operands.  B = value tile, K-major, no swizzle: R rows x 16 k,
-// core matrix = 8 rows x 8 k, k step LBO = 128 B, rows step SBO = 256 B; the
-// host stores each tile's values in exactly this image.  A = B panel (gathered
-// B rows x 128 columns), MN-major, 128-byte swizzled atoms of 8 k-rows x 64
-// columns written by TMA.  One pipeline stage holds TPS = 4 tiles (K = 64): per
-// 64-column half, 8 atoms of 1 KB, so a tile's descriptor has SBO = 1 KB
-// (next 8 k-rows) and LBO = 8 KB (next column half).  One lane fills a stage
-// with, per column half, a single 64 x 64 TMA box when the stage's 64 B rows
-// are consecutive (dense windows), else per tile a 64 x 16 box (16 consecutive
-// rows) or four tile::gather4 loads of 4 rows, plus one cp.async.bulk of the
-// stage's value tiles; the 2-D tensor maps over B write the swizzle and
-// zero-fill columns past N.  The MMA thread issues the stage's 4 MMAs and one
-// commit, so the barrier round trips are paid per K = 64, not per K = 16.
+// core matrices of 8 rows x 16 bytes, 16-byte k chunks LBO = 128 B apart, 8-row
+// groups SBO apart (256 B for 16-bit types, 512 B for tf32); the host stores each
+// tile's values in exactly this image.  A = B panel (gathered B rows x 128
+// columns), MN-major, swizzled 128-byte atom rows written by TMA, in pieces of 64
+// (16-bit) or 32 (fp32) columns.  One pipeline stage is 16 KB of panel (4 tiles
+// of 16-bit, 2 of tf32) + 4 KB of values.  One lane fills a stage with, per
+// piece, a single TMA box of all the stage's rows when they are consecutive
+// (dense windows), else per tile a box of 16 rows (16 consecutive rows) or four
+// tile::gather4 loads of 4 rows, plus one cp.async.bulk of the stage's value
+// tiles; the 2-D tensor maps over B write the swizzle and zero-fill columns past
+// N.  The MMA thread issues the stage's MMAs (4 of K = 16, or 4 of K = 8) and one
+// commit, so the barrier round trips are paid per stage.
 //
 // Warp roles: warps 0-3 epilogue (tcgen05.ld of TMEM lanes 32w..32w+31 ->
 // coalesced fp32 C rows), warp 4 TMEM allocation + MMA issue (one thread),

@@ -76,17 +76,17 @@ int main(int argc, char **argv)
         else if (a == "--seed") seed = std::strtoull(next(), nullptr, 10);
         else if (a == "-d") {
             std::string d = next();
-            dt = d == "f32" ? TCASPMM_F32 : d == "bf16" ? TCASPMM_BF16 : TCASPMM_F16;
+            dt = d == "f32" ? TCASPMM_F32 : d == "tf32" ? TCASPMM_TF32 : d == "bf16" ? TCASPMM_BF16 : TCASPMM_F16;
         } else path = argv[i];
     }
     if (!path) {
-        std::puts("Usage : ./test {matrix.smtx} [-n N] [-d f16|bf16|f32] [-i iters] [-g gpus] [--seed S]");
+        std::puts("Usage : ./test {matrix.smtx} [-n N] [-d f16|bf16|f32|tf32] [-i iters] [-g gpus] [--seed S]");
         return EXIT_FAILURE;
     }
     tcaspmm_csr A;
     TK(tcaspmm_smtx_read(path, &A));
     const int64_t M = A.nrow, K = A.ncol, nnz = A.nnz;
-    const int elem = dt == TCASPMM_F32 ? 4 : 2;
+    const int elem = (dt == TCASPMM_F32 || dt == TCASPMM_TF32) ? 4 : 2;
     std::printf("Input file - %s\n", path);
 
     std::vector<char> hB((size_t)(K * N * elem) + 16);
@@ -199,7 +199,8 @@ int main(int argc, char **argv)
                 "\"gpus\": %d, \"ms\": {\"ours\": %.6f, \"cusparse\": %.6f, \"gemm_cublas\": %.6f}, "
                 "\"gflops\": %.3f, \"algorithmic_bytes\": %lld, \"tc_windows\": %lld, \"residue_nnz\": %lld}\n",
                 path, (long long)M, (long long)K, (long long)N, (long long)nnz,
-                dt == TCASPMM_F32 ? "f32" : dt == TCASPMM_F16 ? "f16" : "bf16", gpus, e_our, e_cusparse, e_gemm,
+                dt == TCASPMM_F32 ? "f32" : dt == TCASPMM_TF32 ? "tf32" : dt == TCASPMM_F16 ? "f16" : "bf16", gpus, e_our,
+                e_cusparse, e_gemm,
                 e_our > 0 ? flops / (e_our * 1e6) : 0.0, (long long)st.algorithmic_bytes, (long long)st.tc_windows,
                 (long long)st.residue_nnz);
     for (int g = 0; g < gpus; g++) {
