@@ -4,7 +4,8 @@
 
 ``crow`` (int32/int64, M+1), ``col`` (int32/int64, nnz) and ``val`` (nnz) describe A in
 CSR on the host or on X's device; ``X`` is a CUDA tensor (K x N, float32 / float16 /
-bfloat16).  The op runs tcaspmm's plan-based C-ABI path (``spmm_b200/lib/libtcaspmm.so``)
+bfloat16; float32 X uses the TF32 tensor-core path when
+``torch.backends.cuda.matmul.allow_tf32`` is set, as PyTorch's own matmuls do).  The op runs tcaspmm's plan-based C-ABI path (``spmm_b200/lib/libtcaspmm.so``)
 on X's current stream: a plan (host preprocessing + one upload of A) is built the
 first time a given (A, N, dtype, device) is seen and reused afterwards, so a GNN layer
 pays the preprocessing once per graph.  The gradient with respect to X is
@@ -32,7 +33,7 @@ _MAX_PLANS = 16
 
 def _key(crow: torch.Tensor, col: torch.Tensor, val: torch.Tensor, N: int, dt, dev: int, transposed: bool) -> Tuple:
     return (crow.data_ptr(), col.data_ptr(), val.data_ptr(), tuple(crow.shape), tuple(col.shape), crow.device.type,
-            int(N), str(dt), dev, transposed, getattr(val, "_version", 0))
+            int(N), dt.name, dev, transposed, getattr(val, "_version", 0))
 
 
 def _host_csr(crow: torch.Tensor, col: torch.Tensor, val: torch.Tensor, ncol: int, transposed: bool) -> CSR:
@@ -52,6 +53,8 @@ def _host_csr(crow: torch.Tensor, col: torch.Tensor, val: torch.Tensor, ncol: in
 
 def _plan(crow, col, val, ncol: int, X: torch.Tensor, transposed: bool) -> Plan:
     dt = as_dtype(X.dtype)
+    if dt == as_dtype("f32") and torch.backends.cuda.matmul.allow_tf32:
+        dt = as_dtype("tf32")  # PyTorch's TF32 switch: fp32 X through the TF32 tensor-core windows
     dev = X.device.index if X.device.index is not None else torch.cuda.current_device()
     k = _key(crow, col, val, X.shape[1], dt, dev, transposed)
     p = _PLANS.get(k)

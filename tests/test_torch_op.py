@@ -97,3 +97,25 @@ def test_sage_mean_layer_with_bias():
     assert oracle.rel_l2(Y.detach().cpu().numpy(), mean) <= 1e-5
     Y.sum().backward()
     assert bias.grad is not None and torch.allclose(bias.grad, torch.full_like(bias, A.nrow))
+
+
+@pytest.mark.gpu
+def test_allow_tf32_routes_fp32_through_tf32_windows():
+    A = T.gen_uniform(1024, 512, 0.3, 2)
+    crow, col, val = torch.from_numpy(A.row_ptr), torch.from_numpy(A.col), torch.from_numpy(A.values())
+    X = torch.randn(512, 64, generator=torch.Generator().manual_seed(3)).cuda()
+    ref = oracle.spmm_f64(A.row_ptr, A.col, A.values(), X.cpu().numpy())
+    old = torch.backends.cuda.matmul.allow_tf32
+    try:
+        torch_op.clear_plan_cache()
+        torch.backends.cuda.matmul.allow_tf32 = False
+        Y32 = torch.ops.tcaspmm.spmm(crow, col, val, X)
+        torch.backends.cuda.matmul.allow_tf32 = True
+        Ytf = torch.ops.tcaspmm.spmm(crow, col, val, X)
+        dts = {k[7] for k in torch_op._PLANS}
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old
+        torch_op.clear_plan_cache()
+    assert oracle.rel_l2(Y32.cpu().numpy(), ref) <= 1e-5
+    assert oracle.rel_l2(Ytf.cpu().numpy(), ref) <= 5e-3
+    assert dts == {"f32", "tf32"}
