@@ -129,11 +129,14 @@ tcaspmm_status build_schedule(const tcaspmm_csr &A, int64_t ncols, tcaspmm_dtype
     for (int64_t r = 0; r < M; r++)
         if (!in_tc(r)) W += (A.row_ptr[r + 1] - A.row_ptr[r]) + BETA;
     const int64_t target_warps = (int64_t)opt.num_sms * env_int("TCASPMM_WARPS_PER_SM", 32);
-    // Per-group budget: W spread over the target warps, within [lo, hi] where hi
-    // keeps a warp's total near 1024 nonzeros whatever P is (measured on GCN at
-    // N = 16, P = 8: 0.54 ms with 1024 per warp against 0.67 ms with 8192).
+    // Per-group budget: W spread over the target warps, within [lo, hi].  With
+    // one or two groups per warp hi is 1024 per group; with more, hi keeps a
+    // warp's total near 1024 nonzeros (measured on GCN: N = 16, P = 8, 0.55 ms
+    // against 0.67 ms with 1024 per group; N = 32, P = 4, 0.71 against 0.79; but
+    // P = 2 is faster at 1024 per group: f16 N = 128 1.45 against 1.59 ms).
     int64_t base = W / std::max<int64_t>(1, (int64_t)P * target_warps);
-    const int64_t hi = std::max<int64_t>(16, env_int("TCASPMM_BUDGET_MAX", 1024) / P);
+    const int64_t bmax = env_int("TCASPMM_BUDGET_MAX", 1024);
+    const int64_t hi = P <= 2 ? bmax : std::max<int64_t>(16, bmax / P);
     const int64_t lo = std::min<int64_t>(env_int("TCASPMM_BUDGET_MIN", 128), hi);
     base = std::min<int64_t>(std::max<int64_t>(base, lo), hi);
     const int64_t warp_budget = base * P;  // a warp runs P rows (or P nnz streams) at once

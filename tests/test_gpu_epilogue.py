@@ -15,7 +15,7 @@ import spmm_b200 as T
 
 pytestmark = pytest.mark.gpu
 
-_TORCH = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+_TORCH = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16, "tf32": torch.float32}
 _OUT_TOL = {"f32": 0.0, "f16": 2.0 ** -11, "bf16": 2.0 ** -8}
 
 
@@ -79,11 +79,11 @@ CASES = {
 
 
 @pytest.mark.parametrize("case", sorted(CASES))
-@pytest.mark.parametrize("dt,N", [("f16", 128), ("f32", 64), ("bf16", 40)])
+@pytest.mark.parametrize("dt,N", [("f16", 128), ("f32", 64), ("bf16", 40), ("tf32", 96)])
 @pytest.mark.parametrize("out", ["f32", "bf16", "f16"])
 def test_scale_bias_relu(case, dt, N, out):
     st = _check(CASES[case](), N, dt, out, scale=_scale, bias=_bias, relu=True)
-    if case == "c1" and dt != "f32" and N % 8 == 0:
+    if case == "c1" and dt != "f32" and N % 8 == 0:  # 16-bit and tf32 take the tensor cores
         assert st["tc_windows"] > 0
     if case == "skew":
         assert st["residue_segments"] > 0
