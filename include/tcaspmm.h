@@ -1,6 +1,7 @@
 /*
  * tcaspmm — B200-native SpMM, C = A * B, CSR A (M x K), dense row-major B (K x N),
- * fp32 C (M x N, row-major, overwritten).  C-ABI boundary of libtcaspmm.so.
+ * fp32 C (M x N, row-major, overwritten; optionally through a fused epilogue).
+ * C-ABI boundary of libtcaspmm.so.
  *
  * Every entry point returns a tcaspmm_status (never exits), except
  * our_spmm_balanced, which keeps the reference's void signature and its
@@ -33,9 +34,9 @@ typedef enum tcaspmm_status {
     TCASPMM_ERR_NO_DEVICE = 8    /* no CUDA device (or fewer than requested) */
 } tcaspmm_status;
 
-/* Element type of B (and of the device copy of A's values). C is always fp32.
- * fp32 runs the CUDA-core path in fp32; f16/bf16 use the tensor-core tiles for
- * dense windows with fp32 accumulation. */
+/* Element type of B (and of the device copy of A's values). C is fp32 (or, with
+ * an epilogue, fp16 / bf16).  fp32 runs the CUDA-core path in fp32; f16 / bf16 /
+ * tf32 use the tensor-core tiles for dense windows with fp32 accumulation. */
 typedef enum tcaspmm_dtype {
     TCASPMM_F32 = 0,
     TCASPMM_F16 = 1,
