@@ -210,8 +210,9 @@ def test_tensor_core_partial_window_and_block():
     assert st["tc_windows"] > 0
 
 
-def test_tensor_core_unaligned_b_falls_back_to_cuda_cores():
-    _, st = check(T.gen_uniform(256, 256, 0.4, 12), 64, "f16", ldb_pad=3)
+@pytest.mark.parametrize("dt", ["f16", "tf32"])
+def test_tensor_core_unaligned_b_falls_back_to_cuda_cores(dt):
+    _, st = check(T.gen_uniform(256, 256, 0.4, 12), 64, dt, ldb_pad=3)
     assert st["tc_windows"] > 0
 
 
