@@ -220,9 +220,11 @@ def main():
                     help="fused epilogue: C = relu(row_scale * (A B) + bias) stored as bf16")
     ap.add_argument("--gather", action="store_true",
                     help="also time the step followed by an NCCL all-gather of C (N > 1)")
-    ap.add_argument("--split", default="columns", choices=["columns", "rows"],
-                    help="multi-GPU partition: column blocks of B/C (A replicated) or row blocks of A/C "
-                         "(B replicated)")
+    ap.add_argument("--split", default="columns", choices=["columns", "rows", "2d"],
+                    help="multi-GPU partition: column blocks of B/C (A replicated), row blocks of A/C "
+                         "(B replicated), or a 2-D grid of both (--grid)")
+    ap.add_argument("--grid", default=None,
+                    help="RxC shard grid for --split 2d (default: two column blocks when N GPUs is even)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     wl = WORKLOADS[args.workload]
@@ -255,13 +257,24 @@ def main():
     A = build(T)
     M, K, nnz = A.nrow, A.ncol, A.nnz
     Bfull = T.gen_dense(K, N, 1, dt)  # host, dt (bf16 as uint16 bits)
+    grid = None
+    if args.split == "2d":
+        if args.grid:
+            grid = tuple(int(x) for x in args.grid.lower().split("x"))
+        else:
+            gc = 2 if world % 2 == 0 else 1
+            grid = (world // gc, gc)
+        if grid[0] * grid[1] != world:
+            raise SystemExit(f"bench: grid {grid} does not match {world} GPUs")
     if args.split == "columns":
         col0, ncols = T.partition_columns(N, dt, world, rank)
         row0, mrows = 0, M
+    elif args.split == "2d":
+        col0, ncols = T.partition_columns(N, dt, grid[1], rank % grid[1])
     else:
         col0, ncols = 0, N
-    plan = T.Plan(A, N, dt, rank=rank, world=world, device=local, split=args.split)
-    if args.split == "rows":
+    plan = T.Plan(A, N, dt, rank=rank, world=world, device=local, split=args.split, grid=grid)
+    if args.split in ("rows", "2d"):
         row0, mrows = plan.shard_rows(0)
     pst = plan.stats
     Bblk = np.ascontiguousarray(Bfull[:, col0:col0 + ncols])
@@ -344,7 +357,7 @@ def main():
     # ---- optional: the step followed by the all-gather of C over NVLink (NCCL), so
     # every rank holds the whole M x N product; reported beside value, not in it ----
     gather = None
-    if args.gather and world > 1:
+    if args.gather and world > 1 and args.split != "2d":
         if args.split == "rows":
             counts = [None] * world
             dist.all_gather_object(counts, int(mrows))
@@ -418,7 +431,8 @@ def main():
     torch.cuda.synchronize(dev)
     ms_e2e = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
     del Bds[1], Cds[1]
-    h2d = K * N * elem * (world if args.split == "rows" else 1)  # row split: every rank copies all of B
+    # Row split: every rank copies all of B; 2-D: every row block copies all of B.
+    h2d = K * N * elem * (world if args.split == "rows" else grid[0] if args.split == "2d" else 1)
     d2h = M * N * (2 if args.epilogue else 4)
 
     # ---- library baselines on this rank's block (reported, not targets), timed
@@ -477,7 +491,10 @@ def main():
             "config": {"workload": desc, "M": M, "K": K, "N": N, "nnz": nnz,
                        "parallelism": f"column shards x{world} (A replicated, no data-path collective)"
                        if args.split == "columns" else
-                       f"row shards x{world} (A split by rows, B replicated, no data-path collective)",
+                       f"row shards x{world} (A split by rows, B replicated, no data-path collective)"
+                       if args.split == "rows" else
+                       f"2-D shards {grid[0]}x{grid[1]} (row blocks of A x column blocks of B, no data-path "
+                       f"collective)",
                        "l2": "flushed between steps (2x L2 buffer)" if flush is not None
                        else "inputs larger than L2 (126 MB)",
                        "launch": "CUDA graph of the plan's launches",

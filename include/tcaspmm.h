@@ -195,6 +195,16 @@ tcaspmm_status tcaspmm_plan_create_rows(const tcaspmm_csr *A, int64_t N, tcaspmm
 /* One process per GPU: the plan of rank's row block only, on `device`. */
 tcaspmm_status tcaspmm_plan_create_rows_shard(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt, int rank,
                                               int world, int device, tcaspmm_plan **out);
+/* 2-D plans: grid_rows x grid_cols shards; shard s = (s / grid_cols, s % grid_cols)
+ * holds row block s / grid_cols of tcaspmm_partition_rows(A, grid_rows) and column
+ * block s % grid_cols of tcaspmm_partition_columns(N, dt, grid_cols, .): each GPU
+ * streams part of A and copies part of B.  dB[s] is the K x col_count block of B,
+ * dC[s] the row_count x col_count block of C. */
+tcaspmm_status tcaspmm_plan_create_2d(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt, int grid_rows,
+                                      int grid_cols, const int *devices, tcaspmm_plan **out);
+/* One process per GPU: the plan of shard `rank` of the grid, on `device`. */
+tcaspmm_status tcaspmm_plan_create_2d_shard(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt, int rank,
+                                            int grid_rows, int grid_cols, int device, tcaspmm_plan **out);
 /* Shard s's row block [row_begin, row_begin + row_count) (0 and M for column-split plans). */
 tcaspmm_status tcaspmm_plan_shard_rows(const tcaspmm_plan *plan, int shard, int64_t *row_begin,
                                        int64_t *row_count);

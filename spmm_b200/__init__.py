@@ -143,6 +143,8 @@ _sig("tcaspmm_partition_rows", [_P(_CSR), C.c_int, _P(_i64)])
 _sig("tcaspmm_plan_create_rows", [_P(_CSR), _i64, C.c_int, C.c_int, _P(C.c_int), _P(_vp)])
 _sig("tcaspmm_plan_create_rows_shard", [_P(_CSR), _i64, C.c_int, C.c_int, C.c_int, C.c_int, _P(_vp)])
 _sig("tcaspmm_plan_shard_rows", [_vp, C.c_int, _P(_i64), _P(_i64)])
+_sig("tcaspmm_plan_create_2d", [_P(_CSR), _i64, C.c_int, C.c_int, C.c_int, _P(C.c_int), _P(_vp)])
+_sig("tcaspmm_plan_create_2d_shard", [_P(_CSR), _i64, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _P(_vp)])
 _sig("tcaspmm_plan_destroy", [_vp])
 _sig("tcaspmm_plan_get_stats", [_vp, _P(_Stats)])
 _sig("tcaspmm_plan_shard", [_vp, C.c_int, _P(C.c_int), _P(_i64), _P(_i64)])
@@ -348,17 +350,29 @@ class Plan:
 
     def __init__(self, A: CSR, N: int, dt="f16", num_gpus: int = 1, devices: Optional[Sequence[int]] = None,
                  *, rank: Optional[int] = None, world: Optional[int] = None, device: Optional[int] = None,
-                 split: str = "columns"):
+                 split: str = "columns", grid: Optional[Sequence[int]] = None):
         """split="columns": shards own column blocks of B and C (A replicated);
-        split="rows": shards own row blocks of A and C (B replicated)."""
-        if split not in ("columns", "rows"):
-            raise ValueError(f"split must be 'columns' or 'rows', not {split!r}")
+        split="rows": shards own row blocks of A and C (B replicated);
+        split="2d": a grid = (row blocks, column blocks) of shards, shard s owning row
+        block s // grid[1] and column block s % grid[1]."""
+        if split not in ("columns", "rows", "2d"):
+            raise ValueError(f"split must be 'columns', 'rows' or '2d', not {split!r}")
+        if split == "2d" and (grid is None or len(grid) != 2):
+            raise ValueError("split='2d' needs grid=(row blocks, column blocks)")
         self._h = _vp()
         self.dt = as_dtype(dt)
         self.split = split
         self.N, self.M, self.K, self.nnz = int(N), A.nrow, A.ncol, A.nnz
         cA = A._c()
-        if rank is not None:
+        if split == "2d":
+            gr, gc = int(grid[0]), int(grid[1])
+            if rank is not None:
+                _check(lib.tcaspmm_plan_create_2d_shard(C.byref(cA), N, int(self.dt), rank, gr, gc, device,
+                                                        C.byref(self._h)))
+            else:
+                devs = (C.c_int * len(devices))(*devices) if devices is not None else None
+                _check(lib.tcaspmm_plan_create_2d(C.byref(cA), N, int(self.dt), gr, gc, devs, C.byref(self._h)))
+        elif rank is not None:
             fn = lib.tcaspmm_plan_create_shard if split == "columns" else lib.tcaspmm_plan_create_rows_shard
             _check(fn(C.byref(cA), N, int(self.dt), rank, world, device, C.byref(self._h)))
         else:
@@ -368,7 +382,11 @@ class Plan:
             fn = lib.tcaspmm_plan_create if split == "columns" else lib.tcaspmm_plan_create_rows
             _check(fn(C.byref(cA), N, int(self.dt), num_gpus, devs, C.byref(self._h)))
         # Nonzeros per shard (row blocks hold part of A).
-        if split == "rows":
+        if split == "2d":
+            rb = partition_rows(A, gr)
+            parts = [rank] if rank is not None else range(gr * gc)
+            self._shard_nnz = [int(A.row_ptr[rb[i // gc + 1]] - A.row_ptr[rb[i // gc]]) for i in parts]
+        elif split == "rows":
             rb = partition_rows(A, world if rank is not None else num_gpus)
             parts = [rank] if rank is not None else range(num_gpus)
             self._shard_nnz = [int(A.row_ptr[rb[i + 1]] - A.row_ptr[rb[i]]) for i in parts]

@@ -264,9 +264,11 @@ static tcaspmm_status create_common(const tcaspmm_csr *A, int64_t N, tcaspmm_dty
     st.ncols_total = N;
     st.num_shards = (int32_t)P->shards.size();
     st.window_rows = S.tc.R;
-    // Column shards share one schedule (shard 0 speaks for all); row shards
-    // add up.
-    for (size_t i = 0; i < (split_rows ? P->shards.size() : 1); i++) {
+    // Column shards of one row block share a schedule (the first column block
+    // speaks for the others); row blocks add up.
+    for (size_t i = 0; i < P->shards.size(); i++) {
+        st.device_bytes = std::max<int64_t>(st.device_bytes, P->shards[i]->bytes);
+        if (split_rows ? P->shards[i]->col_begin != 0 : i != 0) continue;
         const Schedule &Si = P->shards[i]->sched;
         st.tc_windows += (int64_t)Si.tc.windows.size();
         st.tc_tiles += Si.tc.KT ? (int64_t)Si.tc.tile_cols.size() / Si.tc.KT : 0;
@@ -275,7 +277,6 @@ static tcaspmm_status create_common(const tcaspmm_csr *A, int64_t N, tcaspmm_dty
         st.residue_row_warps += (int64_t)Si.res.ranges.size();
         st.residue_segments += (int64_t)Si.res.segs.size();
         st.long_rows += (int64_t)Si.res.longs.size();
-        st.device_bytes = std::max<int64_t>(st.device_bytes, P->shards[i]->bytes);
     }
     st.preprocess_ms = prep;
     st.upload_ms = total - prep;
@@ -386,6 +387,47 @@ tcaspmm_status tcaspmm_plan_create_rows_shard(const tcaspmm_csr *A, int64_t N, t
     std::vector<int64_t> rb(world + 1);
     if ((s = tcaspmm_partition_rows(A, world, rb.data())) != TCASPMM_OK) return s;
     return create_common(A, N, dt, devs, {0}, {N}, out, {rb[rank]}, {rb[rank + 1] - rb[rank]});
+}
+
+tcaspmm_status tcaspmm_plan_create_2d(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt, int grid_rows,
+                                      int grid_cols, const int *devices, tcaspmm_plan **out)
+{
+    clear_error();
+    tcaspmm_status s = check_inputs(A, N, dt, out);
+    if (s != TCASPMM_OK) return s;
+    if (grid_rows < 1 || grid_cols < 1)
+        return fail(TCASPMM_ERR_INVALID_ARG, "plan_create_2d: grid %d x %d", grid_rows, grid_cols);
+    const int g = grid_rows * grid_cols;
+    std::vector<int> devs;
+    if ((s = device_count_check(g, devices, &devs)) != TCASPMM_OK) return s;
+    std::vector<int64_t> rb(grid_rows + 1);
+    if ((s = tcaspmm_partition_rows(A, grid_rows, rb.data())) != TCASPMM_OK) return s;
+    std::vector<int64_t> b(g), c(g), r0(g), rc(g);
+    for (int i = 0; i < g; i++) {
+        const int r = i / grid_cols, q = i % grid_cols;
+        tcaspmm_partition_columns(N, dt, grid_cols, q, &b[i], &c[i]);
+        r0[i] = rb[r];
+        rc[i] = rb[r + 1] - rb[r];
+    }
+    return create_common(A, N, dt, devs, b, c, out, r0, rc);
+}
+
+tcaspmm_status tcaspmm_plan_create_2d_shard(const tcaspmm_csr *A, int64_t N, tcaspmm_dtype dt, int rank,
+                                            int grid_rows, int grid_cols, int device, tcaspmm_plan **out)
+{
+    clear_error();
+    tcaspmm_status s = check_inputs(A, N, dt, out);
+    if (s != TCASPMM_OK) return s;
+    if (grid_rows < 1 || grid_cols < 1 || rank < 0 || rank >= grid_rows * grid_cols)
+        return fail(TCASPMM_ERR_INVALID_ARG, "plan_create_2d_shard: rank %d of %d x %d", rank, grid_rows, grid_cols);
+    std::vector<int> devs;
+    if ((s = device_count_check(1, &device, &devs)) != TCASPMM_OK) return s;
+    std::vector<int64_t> rb(grid_rows + 1);
+    if ((s = tcaspmm_partition_rows(A, grid_rows, rb.data())) != TCASPMM_OK) return s;
+    const int r = rank / grid_cols, q = rank % grid_cols;
+    int64_t b = 0, c = 0;
+    tcaspmm_partition_columns(N, dt, grid_cols, q, &b, &c);
+    return create_common(A, N, dt, devs, {b}, {c}, out, {rb[r]}, {rb[r + 1] - rb[r]});
 }
 
 tcaspmm_status tcaspmm_plan_shard_rows(const tcaspmm_plan *plan, int shard, int64_t *row_begin, int64_t *row_count)

@@ -283,6 +283,32 @@ def test_row_split_plan_on_one_device(dt):
         torch.testing.assert_close(Cr, Cd[r0:r0 + rc], rtol=0, atol=0)
 
 
+@pytest.mark.parametrize("dt", ["f32", "f16"])
+def test_2d_plan_on_one_device(dt):
+    """A 2 x 2 grid of shards placed on cuda:0: shard s writes row block s // 2 of
+    column block s % 2; the per-rank form gives the same blocks."""
+    A = _vstack(T.gen_uniform(256, 4096, 0.3, 1), T.gen_rmat(12, 60000, kind="gcn", seed=9))
+    N = 96
+    B = T.gen_dense(A.ncol, N, 4, "f32")
+    Bd = torch.from_numpy(B).to(_torch_dt(dt)).cuda()
+    Cd = torch.full((A.nrow, N), float("nan"), device="cuda")
+    with T.Plan(A, N, dt, devices=[0, 0, 0, 0], split="2d", grid=(2, 2)) as p:
+        blocks = [(p.shard_rows(s), p.shard(s)[1:]) for s in range(4)]
+        p.execute([Bd[:, c0:c0 + cc] for _, (c0, cc) in blocks],
+                  [Cd[r0:r0 + rc, c0:c0 + cc] for (r0, rc), (c0, cc) in blocks])
+        p.sync_check()
+        st = p.stats
+    assert sorted(r for (r, _), _ in blocks) == [0, 0, blocks[2][0][0], blocks[2][0][0]]
+    tol = TOL_TC if st["tc_nnz"] else TOL_CORE
+    assert oracle.rel_l2(Cd.cpu().numpy(), reference(A, B, dt)) <= tol
+    for s, ((r0, rc), (c0, cc)) in enumerate(blocks):
+        Cr = torch.empty((rc, cc), device="cuda")
+        with T.Plan(A, N, dt, rank=s, device=0, split="2d", grid=(2, 2)) as q:
+            q.execute1(Bd[:, c0:c0 + cc], Cr)
+            q.sync_check()
+        torch.testing.assert_close(Cr, Cd[r0:r0 + rc, c0:c0 + cc], rtol=0, atol=0)
+
+
 def test_tensor_core_wait_time_out_is_reported_and_recoverable():
     """A wait that nothing will satisfy ends in TCASPMM_ERR_TIMEOUT, not a hang, and the GPU stays usable."""
     import ctypes
