@@ -227,22 +227,33 @@ __device__ __forceinline__ void emit(const ResidueParams &p, long long r, int c0
 // acc += sum_{j in [b, e)} val[j] * B[col[j]][c0 .. c0+VEC): full chunks of U
 // without predicates (U indices, U independent B loads, U FMAs), then the
 // remainder one nonzero at a time.
-template <typename T, int VEC, int U>
+template <typename T, int VEC, int U, bool PF = false>
 __device__ __forceinline__ void accumulate_lean(const ResidueParams &p, int b, const int e, int c0, float (&acc)[VEC])
 {
     const T *__restrict__ B = static_cast<const T *>(p.B) + c0;
     const T *__restrict__ val = static_cast<const T *>(p.val);
+    int cn[U];  // PF: columns of the next full chunk, loaded one chunk ahead
+    if constexpr (PF) {
+        if (b + U <= e)
+#pragma unroll
+            for (int u = 0; u < U; ++u) cn[u] = __ldg(p.col + b + u);
+    }
     for (; b + U <= e; b += U) {
         int cc[U];
         float vv[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            cc[u] = __ldg(p.col + b + u);
+            cc[u] = PF ? cn[u] : __ldg(p.col + b + u);
             vv[u] = to_f<T>(__ldg(val + b + u));
         }
         Raw<T, VEC> rb[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) load_raw<T, VEC>(B + (long long)cc[u] * p.ldb, rb[u]);
+        if constexpr (PF) {
+            if (b + 2 * U <= e)
+#pragma unroll
+                for (int u = 0; u < U; ++u) cn[u] = __ldg(p.col + b + U + u);
+        }
 #pragma unroll
         for (int u = 0; u < U; ++u) fma_raw<T, VEC>(vv[u], rb[u], acc);
     }
@@ -258,7 +269,7 @@ __device__ __forceinline__ void accumulate_lean(const ResidueParams &p, int b, c
 // run without predicates (U indices, U B loads, U FMAs with a row-end check),
 // the remainder one nonzero at a time; each row is written when the stream
 // passes its end, trailing empty rows too.
-template <typename T, int VEC, int U, bool EPI>
+template <typename T, int VEC, int U, bool EPI, bool PF = false>
 __device__ __forceinline__ void stream_lean(const ResidueParams &p, int r_lo, int r_hi, int c0)
 {
     if (r_lo >= r_hi) return;
@@ -266,6 +277,10 @@ __device__ __forceinline__ void stream_lean(const ResidueParams &p, int r_lo, in
     const T *__restrict__ val = static_cast<const T *>(p.val);
     int r = r_lo;
     int e = __ldg(p.row_ptr + r + 1);
+    // PF: end of the next row, loaded one row ahead, so passing a row end does
+    // not wait on a row-offset load.
+    int e_next = 0;
+    if constexpr (PF) e_next = r + 1 < r_hi ? __ldg(p.row_ptr + r + 2) : 0;
     int j = __ldg(p.row_ptr + r_lo);
     const int jend = __ldg(p.row_ptr + r_hi);
     EpiRegs<VEC, EPI> er;
@@ -280,21 +295,37 @@ __device__ __forceinline__ void stream_lean(const ResidueParams &p, int r_lo, in
 #pragma unroll
             for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
             ++r;  // < r_hi: nonzero jj < jend lies in a later row
-            e = __ldg(p.row_ptr + r + 1);
+            if constexpr (PF) {
+                e = e_next;
+                if (r + 1 < r_hi) e_next = __ldg(p.row_ptr + r + 2);
+            } else {
+                e = __ldg(p.row_ptr + r + 1);
+            }
             er.load_scale(p, r);
         }
     };
+    int cn[U];  // PF: columns of the next full chunk, loaded one chunk ahead
+    if constexpr (PF) {
+        if (j + U <= jend)
+#pragma unroll
+            for (int u = 0; u < U; ++u) cn[u] = __ldg(p.col + j + u);
+    }
     for (; j + U <= jend; j += U) {
         int cc[U];
         float vv[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            cc[u] = __ldg(p.col + j + u);
+            cc[u] = PF ? cn[u] : __ldg(p.col + j + u);
             vv[u] = to_f<T>(__ldg(val + j + u));
         }
         Raw<T, VEC> rb[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) load_raw<T, VEC>(B + (long long)cc[u] * p.ldb, rb[u]);
+        if constexpr (PF) {
+            if (j + 2 * U <= jend)
+#pragma unroll
+                for (int u = 0; u < U; ++u) cn[u] = __ldg(p.col + j + U + u);
+        }
         if (j + U <= e) {  // the whole chunk lies in the current row: no row-end checks
 #pragma unroll
             for (int u = 0; u < U; ++u) fma_raw<T, VEC>(vv[u], rb[u], acc);
@@ -334,12 +365,12 @@ __device__ __forceinline__ int first_row_at(const int32_t *row_ptr, int lo, int 
     return lo;
 }
 
-// 256 threads, register budget for 4 resident blocks per SM (64 registers):
-// measured faster than 40 registers / 6 blocks and than 80 / 3 on GCN, SAGE and
-// the skew config, the epilogue instantiations included (at 80 registers they
-// ran 25% slower on GCN for the lost occupancy).
-template <typename T, int VEC, int G, int U, bool EPI>
-__global__ void __launch_bounds__(256, 4) residue_kernel(const ResidueParams p)
+// BLOCK threads (256 or 128), register budget of 64 (32 resident warps per SM):
+// measured faster than 40 registers / 48 warps and than 80 / 24 on GCN, SAGE
+// and the skew config, the epilogue instantiations included (at 80 registers
+// they ran 25% slower on GCN for the lost occupancy).
+template <typename T, int VEC, int G, int U, bool EPI, bool PF = false, int BLOCK = 256>
+__global__ void __launch_bounds__(BLOCK, 1024 / BLOCK) residue_kernel(const ResidueParams p)
 {
     constexpr int P = 32 / G;
     constexpr int CPP = G * VEC;  // columns per pass
@@ -360,7 +391,7 @@ __global__ void __launch_bounds__(256, 4) residue_kernel(const ResidueParams p)
             float acc[VEC];
 #pragma unroll
             for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
-            if (c0 < p.ncols) accumulate_lean<T, VEC, U>(p, jb, je, c0, acc);
+            if (c0 < p.ncols) accumulate_lean<T, VEC, U, PF>(p, jb, je, c0, acc);
 #pragma unroll
             for (int off = G; off < 32; off <<= 1)
 #pragma unroll
@@ -420,7 +451,7 @@ __global__ void __launch_bounds__(256, 4) residue_kernel(const ResidueParams p)
     for (int pass = 0; pass < npass; ++pass) {
         const int c0 = pass * CPP + gl * VEC;
         if (c0 >= p.ncols) break;
-        stream_lean<T, VEC, U, EPI>(p, r_lo, r_hi, c0);
+        stream_lean<T, VEC, U, EPI, PF>(p, r_lo, r_hi, c0);
     }
 }
 

@@ -13,11 +13,37 @@ namespace tca {
 // GCN: 1.58 ms at 6 against 1.63 ms at 8).
 template <typename T, bool EPI> constexpr int unroll() { return EPI && sizeof(T) < 4 ? 6 : 8; }
 
+// Launch shape of the residue kernel: BLOCK threads per block, U nonzeros in
+// flight per lane group, PF = columns and row ends loaded one chunk / one row
+// ahead (64 registers hold PF only with U = 6).
+template <typename T, int VEC, int G, bool EPI, bool PF, int BLOCK, int U = unroll<T, EPI>()>
+void launch_res_v(const ResidueParams &p, int total_warps, cudaStream_t st)
+{
+    constexpr int W = BLOCK / 32;
+    const int blocks = (total_warps + W - 1) / W;
+    residue_kernel<T, VEC, G, U, EPI, PF, BLOCK><<<blocks, BLOCK, 0, st>>>(p);
+}
+
+// Vector paths without the epilogue run 128-thread blocks (a finished block's
+// slot is refilled sooner than with 256: 27.3 against 25.8 resident warps per
+// SM on GCN) and, except for one 16-bit group per warp, the prefetching stream.
+// Measured on one B200 against 256 threads, U = 8, no prefetch (ms):
+//   GCN f32 N = 128: 1.92 -> 1.86 (prefetch, two runs averaged; 1.89 without)
+//   GCN f16 N = 128: 1.46 -> 1.35;  GCN f32 N = 64 / 32 / 16: 1.15 / 0.70 /
+//   0.55 -> 1.07 / 0.63 / 0.51;  skew f16 N = 64: 1.26 -> 1.24;
+//   SAGE f16 N = 256 (one 16-bit group per warp): 5.17 -> 5.17 without
+//   prefetch, 5.40 with it.
 template <typename T, int VEC, int G, bool EPI>
 void launch_res(const ResidueParams &p, int total_warps, cudaStream_t st)
 {
-    const int blocks = (total_warps + 7) / 8;
-    residue_kernel<T, VEC, G, unroll<T, EPI>(), EPI><<<blocks, 256, 0, st>>>(p);
+    if constexpr (!EPI && VEC > 1) {
+        if constexpr (G == 32 && sizeof(T) == 2)
+            launch_res_v<T, VEC, G, EPI, false, 128>(p, total_warps, st);
+        else
+            launch_res_v<T, VEC, G, EPI, true, 128, 6>(p, total_warps, st);
+    } else {
+        launch_res_v<T, VEC, G, EPI, false, 256>(p, total_warps, st);
+    }
 }
 
 template <typename T, int VEC, bool EPI>
