@@ -173,6 +173,9 @@ tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB,
     const int total = n_segs + n_ranges;
     if (total == 0 || sh.ncols == 0) return TCASPMM_OK;
     const int elem = dtype_size(dt);
+    // The residue kernel forms B row addresses from a 32-bit row pitch in bytes.
+    if ((uint64_t)ldb * (uint64_t)elem > 0xffffffffull)
+        return fail(TCASPMM_ERR_UNSUPPORTED, "B row pitch of %lld elements exceeds 4 GiB", (long long)ldb);
     // 16-byte vector path needs 16-byte aligned B rows and aligned C rows
     // (16 bytes for fp32 C; 8 or 16 bytes for 16-bit C, VEC = 4 or 8).
     const int out_elem = ep ? ep->out_size() : 4;

@@ -73,6 +73,15 @@ __device__ __forceinline__ void load_raw(const T *p, Raw<T, VEC> &r)
         r.u = __ldg(reinterpret_cast<const uint4 *>(p));
 }
 
+// Start of B row `c` at this lane's columns: Bb points at the lane's first
+// column of row 0 and `pitch` is the row pitch in bytes (< 2^32, checked on the
+// host), so the address is one 32 x 32 -> 64-bit multiply-add.
+template <typename T>
+__device__ __forceinline__ const T *brow(const char *Bb, int c, unsigned pitch)
+{
+    return reinterpret_cast<const T *>(Bb + (unsigned long long)(unsigned)c * pitch);
+}
+
 template <typename T, int VEC>
 __device__ __forceinline__ void zero_raw(Raw<T, VEC> &r)
 {
@@ -230,7 +239,8 @@ __device__ __forceinline__ void emit(const ResidueParams &p, long long r, int c0
 template <typename T, int VEC, int U, bool PF = false>
 __device__ __forceinline__ void accumulate_lean(const ResidueParams &p, int b, const int e, int c0, float (&acc)[VEC])
 {
-    const T *__restrict__ B = static_cast<const T *>(p.B) + c0;
+    const char *Bb = reinterpret_cast<const char *>(static_cast<const T *>(p.B) + c0);
+    const unsigned pitch = (unsigned)(p.ldb * (long long)sizeof(T));
     const T *__restrict__ val = static_cast<const T *>(p.val);
     int cn[U];  // PF: columns of the next full chunk, loaded one chunk ahead
     if constexpr (PF) {
@@ -248,7 +258,7 @@ __device__ __forceinline__ void accumulate_lean(const ResidueParams &p, int b, c
         }
         Raw<T, VEC> rb[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) load_raw<T, VEC>(B + (long long)cc[u] * p.ldb, rb[u]);
+        for (int u = 0; u < U; ++u) load_raw<T, VEC>(brow<T>(Bb, cc[u], pitch), rb[u]);
         if constexpr (PF) {
             if (b + 2 * U <= e)
 #pragma unroll
@@ -260,7 +270,7 @@ __device__ __forceinline__ void accumulate_lean(const ResidueParams &p, int b, c
     for (; b < e; ++b) {
         Raw<T, VEC> rb;
         const float v = to_f<T>(__ldg(val + b));
-        load_raw<T, VEC>(B + (long long)__ldg(p.col + b) * p.ldb, rb);
+        load_raw<T, VEC>(brow<T>(Bb, __ldg(p.col + b), pitch), rb);
         fma_raw<T, VEC>(v, rb, acc);
     }
 }
@@ -273,7 +283,8 @@ template <typename T, int VEC, int U, bool EPI, bool PF = false>
 __device__ __forceinline__ void stream_lean(const ResidueParams &p, int r_lo, int r_hi, int c0)
 {
     if (r_lo >= r_hi) return;
-    const T *__restrict__ B = static_cast<const T *>(p.B) + c0;
+    const char *Bb = reinterpret_cast<const char *>(static_cast<const T *>(p.B) + c0);
+    const unsigned pitch = (unsigned)(p.ldb * (long long)sizeof(T));
     const T *__restrict__ val = static_cast<const T *>(p.val);
     int r = r_lo;
     int e = __ldg(p.row_ptr + r + 1);
@@ -320,7 +331,7 @@ __device__ __forceinline__ void stream_lean(const ResidueParams &p, int r_lo, in
         }
         Raw<T, VEC> rb[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) load_raw<T, VEC>(B + (long long)cc[u] * p.ldb, rb[u]);
+        for (int u = 0; u < U; ++u) load_raw<T, VEC>(brow<T>(Bb, cc[u], pitch), rb[u]);
         if constexpr (PF) {
             if (j + 2 * U <= jend)
 #pragma unroll
@@ -340,7 +351,7 @@ __device__ __forceinline__ void stream_lean(const ResidueParams &p, int r_lo, in
     for (; j < jend; ++j) {
         Raw<T, VEC> rb;
         const float v = to_f<T>(__ldg(val + j));
-        load_raw<T, VEC>(B + (long long)__ldg(p.col + j) * p.ldb, rb);
+        load_raw<T, VEC>(brow<T>(Bb, __ldg(p.col + j), pitch), rb);
         pass_row_ends(j);
         fma_raw<T, VEC>(v, rb, acc);
     }

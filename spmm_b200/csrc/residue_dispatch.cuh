@@ -36,11 +36,17 @@ void launch_res_v(const ResidueParams &p, int total_warps, cudaStream_t st)
 template <typename T, int VEC, int G, bool EPI>
 void launch_res(const ResidueParams &p, int total_warps, cudaStream_t st)
 {
-    if constexpr (!EPI && VEC > 1) {
+    if constexpr (VEC > 1 && !EPI) {
         if constexpr (G == 32 && sizeof(T) == 2)
             launch_res_v<T, VEC, G, EPI, false, 128>(p, total_warps, st);
         else
             launch_res_v<T, VEC, G, EPI, true, 128, 6>(p, total_warps, st);
+    } else if constexpr (VEC > 1) {
+        // Epilogue kernels: the prefetch fits 64 registers only for fp32.
+        if constexpr (sizeof(T) == 4)
+            launch_res_v<T, VEC, G, EPI, true, 128, 6>(p, total_warps, st);
+        else
+            launch_res_v<T, VEC, G, EPI, false, 128>(p, total_warps, st);
     } else {
         launch_res_v<T, VEC, G, EPI, false, 256>(p, total_warps, st);
     }
