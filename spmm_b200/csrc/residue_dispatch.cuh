@@ -24,9 +24,12 @@ void launch_res_v(const ResidueParams &p, int total_warps, cudaStream_t st)
     residue_kernel<T, VEC, G, U, EPI, PF, BLOCK><<<blocks, BLOCK, 0, st>>>(p);
 }
 
-// Vector paths without the epilogue run 128-thread blocks (a finished block's
-// slot is refilled sooner than with 256: 27.3 against 25.8 resident warps per
-// SM on GCN) and, except for one 16-bit group per warp, the prefetching stream.
+// Vector paths run 128-thread blocks (a finished block's slot is refilled
+// sooner than with 256: 27.3 against 25.8 resident warps per SM on GCN) and the
+// prefetching stream, except with one 16-bit group per warp and, for 16-bit
+// types, with the epilogue (its operands leave no registers for the prefetch;
+// GCN f16 with the epilogue 1.56 -> 1.42 ms from the 128-thread blocks and the
+// 32-bit addressing).
 // Measured on one B200 against 256 threads, U = 8, no prefetch (ms):
 //   GCN f32 N = 128: 1.92 -> 1.86 (prefetch, two runs averaged; 1.89 without)
 //   GCN f16 N = 128: 1.46 -> 1.35;  GCN f32 N = 64 / 32 / 16: 1.15 / 0.70 /
