@@ -134,9 +134,12 @@ tcaspmm_status build_schedule(const tcaspmm_csr &A, int64_t ncols, tcaspmm_dtype
     // warp's total near 1024 nonzeros (measured on GCN: N = 16, P = 8, 0.55 ms
     // against 0.67 ms with 1024 per group; N = 32, P = 4, 0.71 against 0.79; but
     // P = 2 is faster at 1024 per group: f16 N = 128 1.45 against 1.59 ms).
+    // With eight or more groups per warp a warp's total is kept near 512
+    // (GCN N = 16 with the prefetching stream: 0.487 against 0.506 ms at 1024;
+    // N = 128 and SAGE are fastest at the 1024 caps, 2048 and 512 both slower).
     int64_t base = W / std::max<int64_t>(1, (int64_t)P * target_warps);
     const int64_t bmax = env_int("TCASPMM_BUDGET_MAX", 1024);
-    const int64_t hi = P <= 2 ? bmax : std::max<int64_t>(16, bmax / P);
+    const int64_t hi = P <= 2 ? bmax : std::max<int64_t>(16, (P >= 8 ? bmax / 2 : bmax) / P);
     const int64_t lo = std::min<int64_t>(env_int("TCASPMM_BUDGET_MIN", 128), hi);
     base = std::min<int64_t>(std::max<int64_t>(base, lo), hi);
     const int64_t warp_budget = base * P;  // a warp runs P rows (or P nnz streams) at once
