@@ -29,7 +29,9 @@ void launch_res_v(const ResidueParams &p, int total_warps, cudaStream_t st)
 // prefetching stream, except with one 16-bit group per warp and, for 16-bit
 // types, with the epilogue (its operands leave no registers for the prefetch;
 // GCN f16 with the epilogue 1.56 -> 1.42 ms from the 128-thread blocks and the
-// 32-bit addressing).
+// 32-bit addressing).  fp32 without the epilogue keeps 7 nonzeros in flight
+// per lane (the most that 64 registers hold with the prefetch): GCN f32 1.765 ->
+// 1.70 ms against 6; 16-bit types keep 6.
 // Measured on one B200 against 256 threads, U = 8, no prefetch (ms):
 //   GCN f32 N = 128: 1.92 -> 1.86 (prefetch, two runs averaged; 1.89 without)
 //   GCN f16 N = 128: 1.46 -> 1.35;  GCN f32 N = 64 / 32 / 16: 1.15 / 0.70 /
@@ -40,7 +42,9 @@ template <typename T, int VEC, int G, bool EPI>
 void launch_res(const ResidueParams &p, int total_warps, cudaStream_t st)
 {
     if constexpr (VEC > 1 && !EPI) {
-        if constexpr (G == 32 && sizeof(T) == 2)
+        if constexpr (sizeof(T) == 4)
+            launch_res_v<T, VEC, G, EPI, true, 128, 7>(p, total_warps, st);
+        else if constexpr (G == 32)
             launch_res_v<T, VEC, G, EPI, false, 128>(p, total_warps, st);
         else
             launch_res_v<T, VEC, G, EPI, true, 128, 6>(p, total_warps, st);
