@@ -15,7 +15,8 @@ template <typename T, bool EPI> constexpr int unroll() { return EPI && sizeof(T)
 
 // Launch shape of the residue kernel: BLOCK threads per block, U nonzeros in
 // flight per lane group, PF = columns and row ends loaded one chunk / one row
-// ahead (64 registers hold PF only with U = 6).
+// ahead.  With PF, 64 registers hold U = 7 for fp32 and U = 6 for 16-bit types
+// (6 for fp32 with the epilogue); beyond that the kernels spill.
 template <typename T, int VEC, int G, bool EPI, bool PF, int BLOCK, int U = unroll<T, EPI>()>
 void launch_res_v(const ResidueParams &p, int total_warps, cudaStream_t st)
 {
@@ -24,20 +25,19 @@ void launch_res_v(const ResidueParams &p, int total_warps, cudaStream_t st)
     residue_kernel<T, VEC, G, U, EPI, PF, BLOCK><<<blocks, BLOCK, 0, st>>>(p);
 }
 
-// Vector paths run 128-thread blocks (a finished block's slot is refilled
-// sooner than with 256: 27.3 against 25.8 resident warps per SM on GCN) and the
-// prefetching stream, except with one 16-bit group per warp and, for 16-bit
-// types, with the epilogue (its operands leave no registers for the prefetch;
-// GCN f16 with the epilogue 1.56 -> 1.42 ms from the 128-thread blocks and the
-// 32-bit addressing).  fp32 without the epilogue keeps 7 nonzeros in flight
-// per lane (the most that 64 registers hold with the prefetch): GCN f32 1.765 ->
-// 1.70 ms against 6; 16-bit types keep 6.
-// Measured on one B200 against 256 threads, U = 8, no prefetch (ms):
-//   GCN f32 N = 128: 1.92 -> 1.86 (prefetch, two runs averaged; 1.89 without)
-//   GCN f16 N = 128: 1.46 -> 1.35;  GCN f32 N = 64 / 32 / 16: 1.15 / 0.70 /
-//   0.55 -> 1.07 / 0.63 / 0.51;  skew f16 N = 64: 1.26 -> 1.24;
-//   SAGE f16 N = 256 (one 16-bit group per warp): 5.17 -> 5.17 without
-//   prefetch, 5.40 with it.
+// Shapes used (all measured on one B200, outputs bit-identical across shapes):
+//   vector paths run 128-thread blocks: a finished block's slot is refilled
+//   sooner than with 256 (27.3 against 25.8 resident warps per SM on GCN);
+//   fp32: prefetch, U = 7 (GCN N = 128: 256 threads / U = 8 / no prefetch 1.92
+//   ms, 128 threads / prefetch / U = 6 1.86, with 32-bit addressing 1.77, U = 7
+//   1.70; N = 64 / 32 / 16: 1.15 / 0.70 / 0.55 -> 1.07 / 0.63 / 0.48);
+//   16-bit, two or more groups per warp: prefetch, U = 6 (GCN f16 N = 128 1.46
+//   -> 1.26 with the addressing; skew N = 64 1.26 -> 1.23);
+//   16-bit, one group per warp (SAGE N = 256): no prefetch, U = 8 (5.17 -> 4.79;
+//   the prefetch at U = 6 was 5.40 before the addressing change, a tie after);
+//   epilogue kernels: prefetch, U = 6 for fp32, none for 16-bit, whose epilogue
+//   operands leave no registers for it (GCN f32 / f16 with the epilogue 1.90 /
+//   1.56 -> 1.68 / 1.42).
 template <typename T, int VEC, int G, bool EPI>
 void launch_res(const ResidueParams &p, int total_warps, cudaStream_t st)
 {
