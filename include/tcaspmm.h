@@ -178,7 +178,18 @@ tcaspmm_status tcaspmm_partition_rows(const tcaspmm_csr *A, int parts, int64_t *
  * A plan holds the preprocessed schedule of A and every device buffer the
  * kernels read (A's CSR arrays, the schedule, tensor-core tiles, scratch).
  * Replaces workload_manager (src/our_spmm.cu:353-477) and the per-call device
- * setup of our_spmm_balanced (src/our_spmm.cu:486-550). */
+ * setup of our_spmm_balanced (src/our_spmm.cu:486-550).
+ *
+ * Schedule tuning, read from the environment when a plan is created (integers;
+ * unset = the measured defaults):
+ *   TCASPMM_DISABLE_TC=1       every row on the CUDA-core residue kernel
+ *   TCASPMM_BUDGET_MAX=1024    cap on a residue warp's nonzeros (per lane group
+ *                              for one or two groups per warp, divided among
+ *                              the groups otherwise, halved from eight groups)
+ *   TCASPMM_BUDGET_MIN=128     floor on a lane group's nonzeros
+ *   TCASPMM_WARPS_PER_SM=32    residue warps per SM the work is spread over
+ * The results stay within the same tolerances whatever these are; long rows may
+ * be summed in a different order. */
 
 /* One plan over num_gpus devices (devices[i], or 0..num_gpus-1 when NULL); the
  * N columns are split by tcaspmm_partition_columns. */
