@@ -172,6 +172,21 @@ def test_partition_rows_covers_rows_in_balanced_blocks(parts):
     assert np.array_equal(T.partition_rows(A, parts), rb)  # deterministic
 
 
+@pytest.mark.parametrize("N", [4, 16, 128])
+@pytest.mark.parametrize("env", [{}, {"TCASPMM_BUDGET_MAX": "64"}, {"TCASPMM_BUDGET_MAX": "4096"},
+                                 {"TCASPMM_WARPS_PER_SM": "4", "TCASPMM_BUDGET_MIN": "16"},
+                                 {"TCASPMM_WARPS_PER_SM": "128"}])
+def test_schedule_coverage_at_narrow_widths_and_tuning_values(N, env, monkeypatch):
+    """The residue schedule covers each nonzero exactly once whatever the lane-group
+    count per warp (N = 4 / 16 / 128 fp32: 32 / 8 / 1 groups) and the tuning variables."""
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    A = T.gen_rmat(13, 60000, kind="gcn", seed=3)
+    cover, _, st = T.schedule_coverage(A, N, "f32")
+    assert np.all(cover == 1), (np.bincount(cover), st)
+    assert st["residue_nnz"] == A.nnz
+
+
 def test_partition_rows_edge_cases():
     empty = T.CSR(0, 5, np.zeros(1, np.int64), np.zeros(0, np.int32), np.zeros(0, np.float32))
     assert list(T.partition_rows(empty, 3)) == [0, 0, 0, 0]
