@@ -94,12 +94,12 @@ def test_c2_sweep(shape, sparsity, kind):
         check(A, N, dt)
 
 
-@pytest.mark.parametrize("dt,N", [("f32", 128), ("f16", 128), ("f32", 16), ("f16", 32)])
+@pytest.mark.parametrize("dt,N", [("f32", 128), ("f16", 128), ("f32", 16), ("f16", 32), ("f32", 8), ("f32", 4), ("bf16", 16)])
 def test_gcn_rmat_small(dt, N):
     check(T.gen_rmat(16, 500000, kind="gcn", seed=2), N, dt)
 
 
-@pytest.mark.parametrize("dt,N", [("f16", 64), ("f32", 64), ("bf16", 8)])
+@pytest.mark.parametrize("dt,N", [("f16", 64), ("f32", 64), ("bf16", 8), ("f32", 8)])
 def test_skew_hub_rows_use_segments(dt, N):
     A = T.gen_skew(300000, 16, 50000, 3.0, seed=4)
     _, st = check(A, N, dt)
