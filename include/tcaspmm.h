@@ -188,8 +188,10 @@ tcaspmm_status tcaspmm_partition_rows(const tcaspmm_csr *A, int parts, int64_t *
  *                              the groups otherwise, halved from eight groups)
  *   TCASPMM_BUDGET_MIN=128     floor on a lane group's nonzeros
  *   TCASPMM_WARPS_PER_SM=32    residue warps per SM the work is spread over
- * The results stay within the same tolerances whatever these are; long rows may
- * be summed in a different order. */
+ * Values are clamped (BUDGET_MAX to [16, 2^20], BUDGET_MIN to [1, 2^20],
+ * WARPS_PER_SM to [1, 1024], DISABLE_TC to [0, 1]); a value that is not a whole
+ * number falls back to the default.  The results stay within the same
+ * tolerances whatever these are; long rows may be summed in a different order. */
 
 /* One plan over num_gpus devices (devices[i], or 0..num_gpus-1 when NULL); the
  * N columns are split by tcaspmm_partition_columns. */

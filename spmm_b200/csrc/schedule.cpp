@@ -34,11 +34,16 @@ void residue_shape(int64_t ncols, tcaspmm_dtype dt, bool vector_path, int *G, in
     *VEC = vec;
 }
 
-static int64_t env_int(const char *name, int64_t dflt)
+// Integer tuning variable, clamped to [lo, hi]; unset, empty or not a whole
+// number (trailing characters included) gives the default.
+static int64_t env_int(const char *name, int64_t dflt, int64_t lo, int64_t hi)
 {
     const char *s = std::getenv(name);
     if (!s || !*s) return dflt;
-    return std::atoll(s);
+    char *end = nullptr;
+    const long long v = std::strtoll(s, &end, 10);
+    if (end == s || *end != '\0') return dflt;
+    return std::min<int64_t>(std::max<int64_t>(v, lo), hi);
 }
 
 // Condensed-tile selection for one window: returns the sorted union of the
@@ -89,7 +94,7 @@ tcaspmm_status build_schedule(const tcaspmm_csr &A, int64_t ncols, tcaspmm_dtype
     const int64_t nwin = (M + R - 1) / R;
     S.win_tc.assign((size_t)nwin, 0);
     const bool tc_ok = opt.allow_tc && dt != TCASPMM_F32 && ncols > 0 && ncols % 8 == 0 &&
-                       env_int("TCASPMM_DISABLE_TC", 0) == 0;
+                       env_int("TCASPMM_DISABLE_TC", 0, 0, 1) == 0;
     if (tc_ok) {
         std::vector<int32_t> cols_u;
         for (int64_t w = 0; w < nwin; w++) {
@@ -128,7 +133,7 @@ tcaspmm_status build_schedule(const tcaspmm_csr &A, int64_t ncols, tcaspmm_dtype
     int64_t W = 0;
     for (int64_t r = 0; r < M; r++)
         if (!in_tc(r)) W += (A.row_ptr[r + 1] - A.row_ptr[r]) + BETA;
-    const int64_t target_warps = (int64_t)opt.num_sms * env_int("TCASPMM_WARPS_PER_SM", 32);
+    const int64_t target_warps = (int64_t)opt.num_sms * env_int("TCASPMM_WARPS_PER_SM", 32, 1, 1024);
     // Per-group budget: W spread over the target warps, within [lo, hi].  With
     // one or two groups per warp hi is 1024 per group; with more, hi keeps a
     // warp's total near 1024 nonzeros (measured on GCN: N = 16, P = 8, 0.55 ms
@@ -138,9 +143,9 @@ tcaspmm_status build_schedule(const tcaspmm_csr &A, int64_t ncols, tcaspmm_dtype
     // (GCN N = 16 with the prefetching stream: 0.487 against 0.506 ms at 1024;
     // N = 128 and SAGE are fastest at the 1024 caps, 2048 and 512 both slower).
     int64_t base = W / std::max<int64_t>(1, (int64_t)P * target_warps);
-    const int64_t bmax = env_int("TCASPMM_BUDGET_MAX", 1024);
+    const int64_t bmax = env_int("TCASPMM_BUDGET_MAX", 1024, 16, 1 << 20);
     const int64_t hi = P <= 2 ? bmax : std::max<int64_t>(16, (P >= 8 ? bmax / 2 : bmax) / P);
-    const int64_t lo = std::min<int64_t>(env_int("TCASPMM_BUDGET_MIN", 128), hi);
+    const int64_t lo = std::min<int64_t>(env_int("TCASPMM_BUDGET_MIN", 128, 1, 1 << 20), hi);
     base = std::min<int64_t>(std::max<int64_t>(base, lo), hi);
     const int64_t warp_budget = base * P;  // a warp runs P rows (or P nnz streams) at once
     RS.long_thr = (int32_t)std::min<int64_t>(INT32_MAX, 2 * base);

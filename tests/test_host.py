@@ -187,6 +187,23 @@ def test_schedule_coverage_at_narrow_widths_and_tuning_values(N, env, monkeypatc
     assert st["residue_nnz"] == A.nnz
 
 
+@pytest.mark.parametrize("env", [{"TCASPMM_BUDGET_MAX": "0"}, {"TCASPMM_BUDGET_MAX": "-5"},
+                                 {"TCASPMM_BUDGET_MAX": "abc"}, {"TCASPMM_BUDGET_MAX": "12x"},
+                                 {"TCASPMM_BUDGET_MIN": "0"}, {"TCASPMM_BUDGET_MIN": "-1"},
+                                 {"TCASPMM_WARPS_PER_SM": "0"}, {"TCASPMM_WARPS_PER_SM": "-3"},
+                                 {"TCASPMM_BUDGET_MAX": "99999999999999999999"}])
+@pytest.mark.parametrize("N", [4, 128])
+def test_out_of_range_tuning_values_are_clamped(env, N, monkeypatch):
+    """Zero, negative, overflowing or non-numeric tuning values must neither crash plan
+    creation (a zero budget used to divide by zero) nor drop a nonzero."""
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    A = T.gen_skew(20000, 4, 5000, 3.0, seed=5)  # hub rows exercise the segment split
+    cover, _, st = T.schedule_coverage(A, N, "f32")
+    assert np.all(cover == 1), (np.bincount(cover), st)
+    assert st["residue_nnz"] == A.nnz
+
+
 def test_partition_rows_edge_cases():
     empty = T.CSR(0, 5, np.zeros(1, np.int64), np.zeros(0, np.int32), np.zeros(0, np.float32))
     assert list(T.partition_rows(empty, 3)) == [0, 0, 0, 0]
