@@ -307,10 +307,15 @@ tcaspmm_status tcaspmm_our_spmm_balanced(const tcaspmm_ref_csr *A_csr, const uin
  * scratch is a fixed 16 MiB array inside the library image, which every GPU
  * that loads the library holds until the process exits.  Limit: two partial
  * rows of N floats (N rounded up to 4) must fit in that array, so N <= 2097152;
- * larger N returns TCASPMM_ERR_UNSUPPORTED.  All calls share the array: calls
- * whose kernels overlap on the GPU race and must be serialised by the caller.
- * The first call on each device looks up the array's device address with that
- * device current; make that first call before any stream capture. */
+ * larger N, and nnz above 2^31 - 65, return TCASPMM_ERR_UNSUPPORTED.  All calls
+ * on one device share that device's array: calls whose kernels overlap on the
+ * GPU race and must be serialised by the caller.  The first call on each device
+ * looks up the array's device address with that device current; with lazy
+ * module loading (the CUDA default since 12.2) that is also when the driver
+ * loads the library's device code and commits the 16 MiB on that device, so the
+ * first call can fail with an out-of-memory error.  Make one warm-up call per
+ * device at initialisation: before any stream capture and before the caller's
+ * memory budget is fixed. */
 tcaspmm_status tcaspmm_spmm_csr_noalloc(const int32_t *d_row_ptr, const int32_t *d_col, const void *d_val,
                                         int64_t M, int64_t K, int64_t nnz, const void *dB, int64_t ldb, float *dC,
                                         int64_t ldc, int64_t N, tcaspmm_dtype dt, void *stream);

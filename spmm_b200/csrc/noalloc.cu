@@ -19,14 +19,18 @@
 // does not depend on timing.
 //
 // The scratch array g_noalloc_carry below (NOALLOC_SCRATCH_BYTES) is held by
-// every GPU that loads this library, until the process exits.  All calls share
-// it: calls whose kernels overlap on the GPU (different streams or threads, or
-// devices sharing nothing else) race on it and must be serialised by the caller.
-// Every scratch slot a call reads is written earlier in the same call, so no
-// part of it has to start at zero, and leftovers of an earlier call are never
-// read.  The first call on each device looks up the array's device address
-// (cudaGetSymbolAddress) with that device current; make that first call before
-// any stream capture.
+// every GPU that loads this library, until the process exits; each device has
+// its own copy.  All calls on one device share that copy: calls whose kernels
+// overlap on the GPU (different streams or host threads) race on it and must be
+// serialised by the caller.  Every scratch slot a call reads is written earlier
+// in the same call, so no part of it has to start at zero, and leftovers of an
+// earlier call are never read.  The first call on each device looks up the
+// array's device address (cudaGetSymbolAddress) with that device current.
+// Under lazy module loading (the CUDA default since 12.2) that first call is
+// also when the driver loads this library's device code and commits the array
+// on the device, so it can fail with out-of-memory; callers make one warm-up
+// call per device at initialisation, before any stream capture and before
+// their memory budget is fixed.
 #include <algorithm>
 #include <climits>
 #include <cstdint>
@@ -46,6 +50,9 @@ constexpr int64_t NOALLOC_SCRATCH_BYTES = 16ll << 20;  // 16 MiB per device
 constexpr int64_t NOALLOC_SCRATCH_FLOATS = NOALLOC_SCRATCH_BYTES / 4;
 constexpr int64_t NOALLOC_MIN_CHUNK = 256;              // nonzeros per warp, at least
 constexpr int NOALLOC_MAX_DEVICES = 64;
+// Nonzero indices are 32-bit in the kernels; the chunk loop reads up to 8 past
+// a chunk start, so nnz stays this far below 2^31.
+constexpr int64_t NOALLOC_MAX_NNZ = (int64_t)INT32_MAX - 64;
 
 // Two partial rows per chunk: [chunk][0] = the chunk's piece of a row that began
 // in an earlier chunk, [chunk][1] = the piece of a row that continues past it.
@@ -100,8 +107,8 @@ __global__ void __launch_bounds__(256) noalloc_chunks(const NoallocParams p)
     const int w = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
     const int lane = threadIdx.x & 31;
     if (w >= p.nchunks) return;
-    const int j0 = w * p.chunk;
-    const int j1 = min(j0 + p.chunk, p.nnz);
+    const int j0 = w * p.chunk;  // < nnz
+    const int j1 = (int)min((long long)j0 + p.chunk, (long long)p.nnz);
     const int r0 = w == 0 ? 0 : row_of(p.row_ptr, p.M, j0);
     const bool head_split = __ldg(p.row_ptr + r0) < j0;
     const T *__restrict__ val = static_cast<const T *>(p.val);
@@ -181,8 +188,8 @@ __global__ void __launch_bounds__(256) noalloc_fixup(const NoallocParams p)
     const int w = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
     const int lane = threadIdx.x & 31;
     if (w == 0 || w >= p.nchunks) return;
-    const int j0 = w * p.chunk;
-    const int j1 = min(j0 + p.chunk, p.nnz);
+    const int j0 = w * p.chunk;  // < nnz
+    const int j1 = (int)min((long long)j0 + p.chunk, (long long)p.nnz);
     const int r0 = row_of(p.row_ptr, p.M, j0);
     const int b = __ldg(p.row_ptr + r0), e = __ldg(p.row_ptr + r0 + 1);
     if (!(b < j0 && e <= j1)) return;
@@ -255,8 +262,9 @@ extern "C" tcaspmm_status tcaspmm_spmm_csr_noalloc(const int32_t *d_row_ptr, con
     if (M < 0 || K < 0 || nnz < 0 || N < 0 || ldb < N || ldc < N)
         return fail(TCASPMM_ERR_INVALID_ARG, "spmm_csr_noalloc: bad sizes M=%lld K=%lld nnz=%lld N=%lld ldb=%lld ldc=%lld",
                     (long long)M, (long long)K, (long long)nnz, (long long)N, (long long)ldb, (long long)ldc);
-    if (M > INT32_MAX - 1 || nnz > INT32_MAX || N > INT32_MAX)
-        return fail(TCASPMM_ERR_UNSUPPORTED, "spmm_csr_noalloc: M, nnz and N must be below 2^31");
+    if (M > INT32_MAX - 1 || nnz > NOALLOC_MAX_NNZ || N > INT32_MAX)
+        return fail(TCASPMM_ERR_UNSUPPORTED, "spmm_csr_noalloc: M and N must be below 2^31 and nnz at most %lld",
+                    (long long)NOALLOC_MAX_NNZ);
     const int64_t cstride = (N + 3) / 4 * 4;
     // Two carry rows per chunk must fit in the fixed scratch.
     const int64_t max_chunks = NOALLOC_SCRATCH_FLOATS / std::max<int64_t>(1, 2 * cstride);

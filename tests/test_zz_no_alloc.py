@@ -41,15 +41,28 @@ def test_rejects_n_beyond_the_fixed_scratch():
     assert "scratch" in T.last_error()
 
 
+def test_rejects_nnz_near_the_32_bit_limit():
+    # Nonzero indices are 32-bit in the kernels: nnz within 64 of 2^31 is refused on the
+    # host, before any pointer is touched.
+    st = _fn(None, None, None, 10, 10, (1 << 31) - 10, None, 8, None, 8, 8, 0, None)
+    assert st == T.Status.UNSUPPORTED
+    assert "nnz" in T.last_error()
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("case,dt,N", [("skew", "f32", 64), ("gcn", "f32", 128), ("c1", "f16", 256),
-                                       ("skew", "bf16", 24), ("empty_rows", "f32", 8)])
+                                       ("skew", "bf16", 24), ("empty_rows", "f32", 8), ("wide", "f32", 4096)])
 def test_noalloc_matches_plan_entry_on_two_calls(case, dt, N):
     import torch
 
     tdt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[dt]
     if case == "skew":
         A = T.gen_skew(200000, 8, 30000, 3.0, seed=21)     # hub rows span many chunks
+    elif case == "wide":
+        # nnz * 2 * N above the 4M floats of scratch: the chunk grows past its 256-nonzero
+        # minimum (about 500 here), so the scratch limit, not the floor, sets the split.
+        A = T.gen_skew(20000, 4, 50000, 3.0, seed=24)
+        assert -(-A.nnz // (4 * 2**20 // (2 * N))) > 256
     elif case == "gcn":
         A = T.gen_rmat(15, 200000, kind="gcn", seed=22)
     elif case == "c1":
@@ -69,11 +82,20 @@ def test_noalloc_matches_plan_entry_on_two_calls(case, dt, N):
         p.sync_check()
     ref = ref.cpu().numpy()
     exact = oracle.spmm_f64(A.row_ptr, A.col, val.float().cpu().numpy(), B.float().cpu().numpy())
+    outs = [torch.full((A.nrow, N), float("nan"), device=dev) for _ in range(2)]
+    torch.cuda.synchronize(dev)
+    free = []
     for call in range(2):                  # second call reuses the scratch left by the first
-        out = torch.full((A.nrow, N), float("nan"), device=dev)
-        _noalloc(rp, col, val, A.nrow, A.ncol, A.nnz, B, out, dt, stream)
+        if call == 1:
+            free.append(torch.cuda.mem_get_info(dev)[0])
+        _noalloc(rp, col, val, A.nrow, A.ncol, A.nnz, B, outs[call], dt, stream)
         torch.cuda.synchronize(dev)
-        got = out.cpu().numpy()
+        if call == 1:
+            free.append(torch.cuda.mem_get_info(dev)[0])
+        got = outs[call].cpu().numpy()
         assert np.isfinite(got).all(), f"call {call}: rows left unwritten"
         assert oracle.rel_l2(got, ref) <= TOL, f"call {call}"
         assert oracle.rel_l2(got, exact) <= TOL, f"call {call}"
+    # The first call may commit the library's device image (lazy loading); after it,
+    # a call must leave the device's free memory exactly where it was.
+    assert free[1] == free[0], f"device free memory moved by {free[0] - free[1]} bytes on the second call"
