@@ -27,13 +27,35 @@ import torch
 
 from . import CSR, Epilogue, Plan, as_dtype
 
-_PLANS: Dict[Tuple, Plan] = {}
+
+class _Entry:
+    """A cached plan and the CSR tensors it was built from.
+
+    The entry keeps those tensors alive, so their memory cannot be handed to a new
+    graph while the plan is cached, and it is reused only for the very same tensor
+    objects at the same versions: an in-place edit of crow, col or val (which bumps
+    the tensor's version counter) or a different tensor at a recycled address both
+    build a new plan."""
+
+    __slots__ = ("plan", "tensors", "versions")
+
+    def __init__(self, plan: Plan, tensors: Tuple[torch.Tensor, ...]):
+        self.plan = plan
+        self.tensors = tensors
+        self.versions = tuple(t._version for t in tensors)
+
+    def matches(self, tensors: Tuple[torch.Tensor, ...]) -> bool:
+        return all(a is b for a, b in zip(self.tensors, tensors)) and \
+            self.versions == tuple(t._version for t in tensors)
+
+
+_PLANS: Dict[Tuple, _Entry] = {}
 _MAX_PLANS = 16
 
 
 def _key(crow: torch.Tensor, col: torch.Tensor, val: torch.Tensor, N: int, dt, dev: int, transposed: bool) -> Tuple:
     return (crow.data_ptr(), col.data_ptr(), val.data_ptr(), tuple(crow.shape), tuple(col.shape), crow.device.type,
-            int(N), dt.name, dev, transposed, getattr(val, "_version", 0))
+            int(N), dt.name, dev, transposed)
 
 
 def _host_csr(crow: torch.Tensor, col: torch.Tensor, val: torch.Tensor, ncol: int, transposed: bool) -> CSR:
@@ -57,18 +79,22 @@ def _plan(crow, col, val, ncol: int, X: torch.Tensor, transposed: bool) -> Plan:
         dt = as_dtype("tf32")  # PyTorch's TF32 switch: fp32 X through the TF32 tensor-core windows
     dev = X.device.index if X.device.index is not None else torch.cuda.current_device()
     k = _key(crow, col, val, X.shape[1], dt, dev, transposed)
-    p = _PLANS.get(k)
-    if p is None:
+    tensors = (crow, col, val)
+    e = _PLANS.get(k)
+    if e is not None and not e.matches(tensors):
+        _PLANS.pop(k).plan.close()  # same addresses and shapes, different or edited tensors
+        e = None
+    if e is None:
         if len(_PLANS) >= _MAX_PLANS:
-            _PLANS.pop(next(iter(_PLANS))).close()
-        p = Plan(_host_csr(crow, col, val, ncol, transposed), X.shape[1], dt, 1, [dev])
-        _PLANS[k] = p
-    return p
+            _PLANS.pop(next(iter(_PLANS))).plan.close()
+        e = _Entry(Plan(_host_csr(crow, col, val, ncol, transposed), X.shape[1], dt, 1, [dev]), tensors)
+        _PLANS[k] = e
+    return e.plan
 
 
 def clear_plan_cache() -> None:
     while _PLANS:
-        _PLANS.popitem()[1].close()
+        _PLANS.popitem()[1].plan.close()
 
 
 @torch.library.custom_op("tcaspmm::spmm", mutates_args=())

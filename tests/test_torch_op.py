@@ -45,6 +45,81 @@ def test_forward_and_backward_match_the_oracle(dt):
     assert oracle.rel_l2(X.grad.float().cpu().numpy(), gref) <= (1e-5 if dt == torch.float32 else 1e-2)
 
 
+def test_plan_cache_entry_matches_only_the_same_unedited_tensors():
+    """A cached plan is reused only for the very tensor objects it was built from, at the
+    versions it saw: an in-place edit or another tensor (even with equal contents, as a
+    new graph at a recycled address would be) does not match."""
+    A, crow, col, val = _graph()
+    e = torch_op._Entry(plan=None, tensors=(crow, col, val))
+    assert e.matches((crow, col, val))
+    assert not e.matches((crow, col.clone(), val))
+    col[0] = col[0]  # an in-place write bumps the version counter, whatever it writes
+    assert not e.matches((crow, col, val))
+    e = torch_op._Entry(plan=None, tensors=(crow, col, val))
+    val.mul_(1.0)
+    assert not e.matches((crow, col, val))
+
+
+def _permuted_graph(crow, col, val, seed):
+    """Same row offsets and shapes, different column indices (and so a different product)."""
+    ncol = int(col.max()) + 1
+    perm = torch.randperm(ncol, generator=torch.Generator().manual_seed(seed))
+    rows = []
+    for r in range(crow.shape[0] - 1):
+        c = perm[col[crow[r]:crow[r + 1]].long()].sort().values
+        rows.append(c)
+    return torch.cat(rows).to(col.dtype)
+
+
+@pytest.mark.gpu
+def test_new_graph_at_recycled_addresses_gets_a_new_plan():
+    """Free a device graph, allocate a different graph of the same shapes (the caching
+    allocator hands back the same addresses), and the op must multiply by the new graph."""
+    A, crow, col, val = _graph(scale=9, edges=4000, seed=8)
+    X = torch.randn(A.ncol, 16, generator=torch.Generator().manual_seed(4)).cuda()
+    torch_op.clear_plan_cache()
+    col2_host = _permuted_graph(crow, col, val, seed=9)
+    d1 = [t.cuda() for t in (crow, col, val)]
+    ptrs = [t.data_ptr() for t in d1]
+    Y1 = torch.ops.tcaspmm.spmm(*d1, X)
+    del d1
+    torch_op.clear_plan_cache()  # nothing holds the first graph any more: its memory is free
+    d2 = [t.cuda() for t in (crow, col2_host, val)]
+    reused = [t.data_ptr() for t in d2] == ptrs
+    Y2 = torch.ops.tcaspmm.spmm(*d2, X)
+    ref2 = oracle.spmm_f64(A.row_ptr, col2_host.numpy(), val.numpy(), X.cpu().numpy())
+    assert oracle.rel_l2(Y2.cpu().numpy(), ref2) <= 1e-5, f"addresses reused: {reused}"
+    assert oracle.rel_l2(Y1.cpu().numpy(), ref2) > 1e-2  # the two graphs differ
+    # With the first graph still cached (it holds its tensors), a second graph of the same
+    # shapes gets its own plan too.
+    d3 = [t.cuda() for t in (crow, col, val)]
+    Y3 = torch.ops.tcaspmm.spmm(*d3, X)
+    ref1 = oracle.spmm_f64(A.row_ptr, A.col, val.numpy(), X.cpu().numpy())
+    assert oracle.rel_l2(Y3.cpu().numpy(), ref1) <= 1e-5
+    torch_op.clear_plan_cache()
+
+
+@pytest.mark.gpu
+def test_in_place_edit_of_the_graph_rebuilds_the_plan():
+    A, crow, col, val = _graph(scale=9, edges=4000, seed=10)
+    X = torch.randn(A.ncol, 16, generator=torch.Generator().manual_seed(5)).cuda()
+    torch_op.clear_plan_cache()
+    dcrow, dcol, dval = crow.cuda(), col.cuda(), val.cuda()
+    Y1 = torch.ops.tcaspmm.spmm(dcrow, dcol, dval, X)
+    ref1 = oracle.spmm_f64(A.row_ptr, A.col, val.numpy(), X.cpu().numpy())
+    assert oracle.rel_l2(Y1.cpu().numpy(), ref1) <= 1e-5
+    col2 = _permuted_graph(crow, col, val, seed=11)
+    dcol.copy_(col2.cuda())                     # edit the columns in place
+    Y2 = torch.ops.tcaspmm.spmm(dcrow, dcol, dval, X)
+    ref2 = oracle.spmm_f64(A.row_ptr, col2.numpy(), val.numpy(), X.cpu().numpy())
+    assert oracle.rel_l2(Y2.cpu().numpy(), ref2) <= 1e-5
+    dval.mul_(2.0)                              # and the values
+    Y3 = torch.ops.tcaspmm.spmm(dcrow, dcol, dval, X)
+    assert oracle.rel_l2(Y3.cpu().numpy(), 2.0 * ref2) <= 1e-5
+    assert len(torch_op._PLANS) == 1            # each edit replaced the stale plan
+    torch_op.clear_plan_cache()
+
+
 @pytest.mark.gpu
 def test_gcn_layer_reuses_its_plan():
     A, crow, col, val = _graph()
