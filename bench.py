@@ -16,6 +16,7 @@ oracle/oracle.c (a restatement of src/our_spmm.cu's arithmetic), run by rank 0.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -134,6 +135,111 @@ def algorithmic_bytes(M, K, nnz, N, elem):
     return (M + 1) * 4 + nnz * (4 + elem) + K * N * elem + M * N * 4
 
 
+class HostGen:
+    """The seeded input generators of libtcaspmm_host.so (host code only: no CUDA runtime,
+    no GPU kernels), so the reference arm builds the same inputs as the GPU arm without
+    loading the product library.  Mirrors the gen_* functions of spmm_b200."""
+
+    class _CSR(ctypes.Structure):
+        _fields_ = [("nrow", ctypes.c_int64), ("ncol", ctypes.c_int64), ("nnz", ctypes.c_int64),
+                    ("row_ptr", ctypes.POINTER(ctypes.c_int64)), ("col_idx", ctypes.POINTER(ctypes.c_int32)),
+                    ("val", ctypes.POINTER(ctypes.c_float))]
+
+    class Matrix:
+        def __init__(self, nrow, ncol, row_ptr, col, val):
+            self.nrow, self.ncol, self.row_ptr, self.col, self.val = nrow, ncol, row_ptr, col, val
+            self.nnz = int(col.shape[0])
+
+        def values(self):
+            return self.val if self.val is not None else np.ones(self.nnz, np.float32)
+
+    def __init__(self):
+        self.lib = ctypes.CDLL(os.path.join(ROOT, "spmm_b200", "lib", "libtcaspmm_host.so"))
+        self.lib.tcaspmm_last_error.restype = ctypes.c_char_p
+
+    def _take(self, st, s):
+        if st != 0:
+            raise RuntimeError(f"generator failed ({st}): {self.lib.tcaspmm_last_error().decode()}")
+        try:
+            rp = np.ctypeslib.as_array(s.row_ptr, shape=(s.nrow + 1,)).copy()
+            col = np.ctypeslib.as_array(s.col_idx, shape=(max(s.nnz, 1),))[: s.nnz].copy()
+            val = np.ctypeslib.as_array(s.val, shape=(max(s.nnz, 1),))[: s.nnz].copy() if bool(s.val) else None
+            return self.Matrix(int(s.nrow), int(s.ncol), rp, col, val)
+        finally:
+            self.lib.tcaspmm_csr_free(ctypes.byref(s))
+
+    def gen_rmat(self, scale, edges, a=0.57, b=0.19, c=0.19, kind="gcn", seed=0):
+        s = self._CSR()
+        f = self.lib.tcaspmm_gen_rmat
+        f.argtypes = [ctypes.c_int, ctypes.c_int64, ctypes.c_double, ctypes.c_double, ctypes.c_double, ctypes.c_int,
+                      ctypes.c_uint64, ctypes.POINTER(self._CSR)]
+        return self._take(f(scale, edges, a, b, c, {"gcn": 0, "sage": 1}[kind], seed, ctypes.byref(s)), s)
+
+    def gen_uniform(self, M, K, density, seed=0):
+        s = self._CSR()
+        f = self.lib.tcaspmm_gen_uniform
+        f.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_double, ctypes.c_uint64, ctypes.POINTER(self._CSR)]
+        return self._take(f(M, K, density, seed, ctypes.byref(s)), s)
+
+    def gen_skew(self, n, hubs, hub_nnz, lam=3.0, seed=0):
+        s = self._CSR()
+        f = self.lib.tcaspmm_gen_skew
+        f.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_double, ctypes.c_uint64,
+                      ctypes.POINTER(self._CSR)]
+        return self._take(f(n, hubs, hub_nnz, lam, seed, ctypes.byref(s)), s)
+
+    def gen_dense(self, rows, cols, seed=0, dt="f32"):
+        code = {"f32": 0, "f16": 1, "bf16": 2, "tf32": 3}[dt]
+        out = np.empty((rows, cols), dtype={0: np.float32, 1: np.float16, 2: np.uint16, 3: np.float32}[code])
+        f = self.lib.tcaspmm_gen_dense
+        f.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_uint64, ctypes.c_int, ctypes.c_void_p]
+        st = f(rows, cols, seed, code, out.ctypes.data)
+        if st != 0:
+            raise RuntimeError(f"gen_dense failed ({st})")
+        return out
+
+
+def _round_to(x: np.ndarray, dt: str) -> np.ndarray:
+    """fp32 values rounded as the plan stores them (f16 / bf16 round to nearest even)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    if dt == "f16":
+        return x.astype(np.float16).astype(np.float32)
+    if dt == "bf16":
+        u = x.view(np.uint32).astype(np.uint64)
+        u = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+        return u.astype(np.uint32).view(np.float32)
+    return x
+
+
+def _as_f32(b: np.ndarray, dt: str) -> np.ndarray:
+    """A host B block in the plan dtype (bf16 as uint16 bits) -> float32."""
+    if dt == "bf16":
+        return (b.astype(np.uint32) << 16).view(np.float32)
+    return b.astype(np.float32)
+
+
+def parity_sample(A, Bblk: np.ndarray, C_rows: np.ndarray, rows: np.ndarray, dt: str, ep_host=None,
+                  chunk: int = 8192) -> float:
+    """rel-L2 of the device rows C_rows (one per entry of `rows`, this rank's column
+    block) against an fp64 sum over each row's nonzeros, computed here in numpy from
+    the same rounded inputs; ep_host = (row_scale, bias) applies the bench's epilogue
+    (relu(s * AB + b)) to the reference."""
+    vals = _round_to(A.values(), dt).astype(np.float64)
+    num = den = 0.0
+    for i, r in enumerate(rows):
+        b, e = int(A.row_ptr[r]), int(A.row_ptr[r + 1])
+        ref = np.zeros(Bblk.shape[1], np.float64)
+        for j in range(b, e, chunk):
+            k = min(e, j + chunk)
+            ref += vals[j:k] @ _as_f32(Bblk[A.col[j:k]], dt).astype(np.float64)
+        if ep_host is not None:
+            rs, bias = ep_host
+            ref = np.maximum(rs[r] * ref + bias, 0.0)
+        num += float(np.sum((C_rows[i].astype(np.float64) - ref) ** 2))
+        den += float(np.sum(ref ** 2))
+    return (num / den) ** 0.5 if den > 0 else (num ** 0.5)
+
+
 def cpu_reference(A, B, threads: int, budget_s: float = 12.0):
     """Time the fp32 CPU CSR loop; whole-matrix passes until budget_s, else a row sample."""
     import oracle
@@ -160,7 +266,6 @@ def run_reference(args, wl):
     Each step is a bounded, strided row sample of the same workload, sized so
     the whole --warmup + --steps run stays within about two minutes."""
     import oracle
-    import spmm_b200 as T
 
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -169,6 +274,7 @@ def run_reference(args, wl):
     if args.dtype:
         dt = args.dtype
         desc += f" [dtype {dt}]"
+    T = HostGen()  # the same seeded inputs, without loading the GPU library
     A = build(T)
     B = T.gen_dense(A.ncol, N, 1, "f32")
     if dt in ("f16", "bf16"):
@@ -354,6 +460,29 @@ def main():
     flops = 2.0 * nnz * N
     value = flops / (ms_step * 1e-3) / 1e9
 
+    # ---- correctness of this rank's C block (outside the timed region): a seeded
+    # sample of its rows, the longest rows included, against an fp64 sum computed on
+    # the host from the same rounded inputs; the worst rank is reported ----
+    rl = np.diff(A.row_ptr[row0:row0 + mrows + 1])
+    g = np.random.default_rng(1234 + rank)
+    hub = row0 + np.argsort(-rl, kind="stable")[:8]
+    rows_s = np.unique(np.concatenate([hub, row0 + g.choice(mrows, size=min(mrows, 2000), replace=False)]))
+    C_rows = Cd[torch.from_numpy(rows_s - row0).to(dev)].float().cpu().numpy()
+    ep_host = None
+    if ep is not None:
+        ep_host = (ep.row_scale.cpu().numpy().astype(np.float64), ep.bias.cpu().numpy().astype(np.float64))
+        ep_rows = np.zeros(M, np.float64)
+        ep_rows[row0:row0 + mrows] = ep_host[0]
+        ep_host = (ep_rows, ep_host[1])
+    rel = parity_sample(A, Bblk, C_rows, rows_s, dt, ep_host)
+    rel = max_over_ranks(rel)
+    # fp32 on the CUDA cores: 1e-5; 16-bit / TF32 inputs through the tensor cores:
+    # 5e-3; bf16 output of the epilogue adds its own rounding (2^-9 relative).
+    tol = 1e-5 if dt == "f32" and ep is None else 5e-3 if ep is None else 8e-3
+    parity = {"rel_l2": float(f"{rel:.3e}"), "tol": tol, "ok": bool(rel <= tol),
+              "rows_per_rank": int(rows_s.shape[0]), "hub_rows_per_rank": 8,
+              "reference": "fp64 host sum over the sampled rows, same rounded inputs", "ranks": world}
+
     # ---- optional: the step followed by the all-gather of C over NVLink (NCCL), so
     # every rank holds the whole M x N product; reported beside value, not in it ----
     gather = None
@@ -516,6 +645,7 @@ def main():
                           "spmm_cusparse_gflops": round(flops / (ms_cusparse * 1e-3) / 1e9, 3)
                           if isinstance(ms_cusparse, float) else None},
             "cpu_baseline": cpu,
+            "parity": parity,
             **({"with_gather": gather} if gather else {}),
             "clocks": sampler.summary(),
             "gpu_launches": kernels_per_step * args.steps * world,
