@@ -1,11 +1,12 @@
-// ./test <matrix.smtx> [-n N] [-d f16|bf16|f32] [-i iters] [-g gpus] [--seed S]
+// ./test <matrix.smtx> [-n N] [-d f16|bf16|f32] [-i iters] [-g gpus] [--seed S] [--dump C.bin]
 //
 // Drop-in for the reference driver (src/test.cu:29-88): loads the .smtx file,
 // builds B (K x N, default N = 256 as src/test.cu:47), runs dense cuBLAS
 // GemmEx (the reference's gold), cuSPARSE SpMM and tcaspmm, validates both
 // against the gold with compare_mat's rule (an element fails only if both its
 // absolute and relative error reach 1e-3, src/general.cuh:71-123), and prints
-// the reference's three timing lines followed by one JSON line.
+// the reference's three timing lines followed by one JSON line.  --dump writes
+// tcaspmm's C (M x N fp32, row-major, little-endian) to a file for external checks.
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
@@ -60,6 +61,7 @@ int main(int argc, char **argv)
     int64_t N = 256;
     int iters = 10, gpus = 1;
     uint64_t seed = 0;
+    const char *dump = nullptr;
     tcaspmm_dtype dt = TCASPMM_F16;
     for (int i = 1; i < argc; i++) {
         std::string a = argv[i];
@@ -74,13 +76,15 @@ int main(int argc, char **argv)
         else if (a == "-i") iters = std::atoi(next());
         else if (a == "-g") gpus = std::atoi(next());
         else if (a == "--seed") seed = std::strtoull(next(), nullptr, 10);
+        else if (a == "--dump") dump = next();
         else if (a == "-d") {
             std::string d = next();
             dt = d == "f32" ? TCASPMM_F32 : d == "tf32" ? TCASPMM_TF32 : d == "bf16" ? TCASPMM_BF16 : TCASPMM_F16;
         } else path = argv[i];
     }
     if (!path) {
-        std::puts("Usage : ./test {matrix.smtx} [-n N] [-d f16|bf16|f32|tf32] [-i iters] [-g gpus] [--seed S]");
+        std::puts("Usage : ./test {matrix.smtx} [-n N] [-d f16|bf16|f32|tf32] [-i iters] [-g gpus] [--seed S] "
+                  "[--dump C.bin]");
         return EXIT_FAILURE;
     }
     tcaspmm_csr A;
@@ -190,6 +194,15 @@ int main(int argc, char **argv)
     e_our = iters ? worst / iters : 0.0;
     if (have_gold && !compare_mat(Cgold.data(), Cmp.data(), M * N, 1e-3f))
         std::printf("\033[35mvalidation failed (Our, balanced)\033[0m\n");
+    if (dump) {
+        FILE *f = std::fopen(dump, "wb");
+        const bool ok = f && std::fwrite(Cmp.data(), sizeof(float), (size_t)(M * N), f) == (size_t)(M * N);
+        if (f) std::fclose(f);
+        if (!ok) {
+            std::fprintf(stderr, "cannot write %s\n", dump);
+            return EXIT_FAILURE;
+        }
+    }
 
     std::printf("GemmEx : \033[36m[%lf] ms\033[0m\n", e_gemm);
     std::printf("cuSPARSE: \033[36m[%lf] ms\033[0m \n", e_cusparse);

@@ -86,7 +86,10 @@ def dense_from_csr(M, K, rp, col, val_bits):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-src", default="/root/reference/src")
+    here = os.path.dirname(os.path.abspath(__file__))
+    default_ref = os.environ.get("TCASPMM_REF_SRC") or os.path.abspath(
+        os.path.join(here, "..", "..", "..", "reference", "src"))  # a reference checkout beside the repo
+    ap.add_argument("--ref-src", default=default_ref)
     args = ap.parse_args()
     lib = load_ref(args.ref_src)
 

@@ -38,3 +38,18 @@ def test_cusparse_csr_matches_the_oracle():
     with T.Plan(A, 64, "f32") as p:
         ms = T.cusparse_spmm(p, Bd, C, warmup=1, iters=2)
     assert ms > 0 and oracle.rel_l2(C.cpu().numpy(), ref) <= 1e-5
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16", "f32"])
+def test_cublas_gold_matches_the_oracle(dt):
+    """The dense cuBLAS GemmEx that the ./test driver uses as its gold (the reference's
+    perform_GemmEx, src/gemm_cublas.cu:3-112): fp32 accumulation of the rounded inputs,
+    so it agrees with the fp64 oracle to fp32 accumulation error."""
+    tdt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}[dt]
+    A = T.gen_uniform(2048, 512, 0.3, 0)  # the C1 weight
+    Bd, ref = _inputs(A, 256, dt)
+    Ad = torch.from_numpy(A.to_scipy().toarray()).to(tdt).cuda()
+    C = torch.full((A.nrow, 256), float("nan"), device="cuda")
+    ms = T.cublas_gemm(Ad, Bd, C, dt, warmup=1, iters=2)
+    assert ms > 0
+    assert oracle.rel_l2(C.cpu().numpy(), ref) <= 1e-5

@@ -85,12 +85,14 @@ def test_c1_ffn_uniform(dt, N):
 
 
 @pytest.mark.parametrize("shape", [(512, 2048), (2048, 2048), (4096, 1024)])
-@pytest.mark.parametrize("sparsity", [0.5, 0.9, 0.98])
+@pytest.mark.parametrize("sparsity", [0.5, 0.7, 0.8, 0.9, 0.95, 0.98])
 @pytest.mark.parametrize("kind", ["uniform", "magnitude"])
 def test_c2_sweep(shape, sparsity, kind):
+    """The full pruned-weight grid of the sweep config: three shapes x six sparsities x
+    two structures, fp16 at N = 64 / 128 / 256 / 512 and fp32 at N = 64 / 256."""
     M, K = shape
     A = T.gen_uniform(M, K, 1 - sparsity, 1) if kind == "uniform" else T.gen_magnitude(M, K, sparsity, 1)
-    for dt, N in (("f16", 128), ("f32", 64)):
+    for dt, N in (("f16", 64), ("f16", 128), ("f16", 256), ("f16", 512), ("f32", 64), ("f32", 256)):
         check(A, N, dt)
 
 
