@@ -24,6 +24,18 @@ inline bool dtype_valid(int dt)
 uint16_t float_to_half_bits(float f);
 uint16_t float_to_bf16_bits(float f);
 float half_bits_to_float(uint16_t h);
+inline float bf16_bits_to_float(uint16_t b)
+{
+    const uint32_t u = (uint32_t)b << 16;
+    float f;
+    __builtin_memcpy(&f, &u, 4);
+    return f;
+}
+
+// ---- tuning variables (read when a plan is created) ----
+// Integer variable clamped to [lo, hi]; unset or not a whole number: dflt.
+int64_t env_int(const char *name, int64_t dflt, int64_t lo, int64_t hi);
+inline bool env_flag(const char *name, bool dflt) { return env_int(name, dflt ? 1 : 0, 0, 1) != 0; }
 
 // ---- counter-based random streams (SplitMix64 finaliser over a counter) ----
 inline uint64_t mix64(uint64_t z)

@@ -133,6 +133,30 @@ tcaspmm_status build_shard(const tcaspmm_csr &Afull, tcaspmm_dtype dt, int devic
             sh->val = d;
         }
     }
+    // Packed {column, value} pairs for the cooperative-chunk kernels, which run
+    // when a warp holds two or more lane groups (narrow column blocks); the
+    // value is the dtype-rounded value widened to fp32 (exact).
+    {
+        int G = 32, VEC = 4;
+        residue_shape(ncols, dt, true, &G, &VEC);
+        sh->coop = G >= 4 && G < 32 && ncols > 0 && A.nnz > 0 && env_flag("TCASPMM_RESIDUE_COOP", true);
+    }
+    if (sh->coop) {
+        const int64_t np = (A.nnz + 15) / 16 * 16 + 16;
+        std::vector<int2> pr((size_t)np, make_int2(0, 0));
+        std::vector<uint16_t> h16;
+        if (!dtype_fp32(dt) && A.val) h16 = to_16bit(A.val, A.nnz, dt);
+#pragma omp parallel for schedule(static)
+        for (int64_t j = 0; j < A.nnz; j++) {
+            float v = A.val ? A.val[j] : 1.0f;
+            if (!h16.empty())
+                v = dt == TCASPMM_F16 ? half_bits_to_float(h16[j]) : bf16_bits_to_float(h16[j]);
+            int vb;
+            std::memcpy(&vb, &v, 4);
+            pr[j] = make_int2(A.col_idx[j], vb);
+        }
+        if ((s = upload(*sh, &sh->pairs, pr.data(), pr.size(), "column/value pairs")) != TCASPMM_OK) return s;
+    }
     // Residue schedule and its scratch (partials + counters).
     const ResidueSchedule &RS = S.res;
     static_assert(sizeof(Int2) == sizeof(int2) && sizeof(Int4) == sizeof(int4), "layout");
@@ -199,15 +223,19 @@ tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB,
     p.segs = (const int4 *)sh.segs;
     p.n_segs = n_segs;
     p.longs = (const int4 *)sh.longs;
+    p.pairs = sh.pairs;
     p.partials = sh.partials;
     p.pstride = sh.pstride;
     p.counters = sh.counters;
     p.ep = EpiParams{nullptr, nullptr, 0, 0};
+    // Cooperative chunks need the pairs and the vector shape they were built for
+    // (the epilogue instantiations never take them).
+    const bool coop = sh.coop && vec && G >= 4 && G < 32 && !ep;
     if (ep) {
         p.ep = EpiParams{ep->row_scale, ep->bias, ep->relu, ep->out};
-        launch_residue_epi(dt, vec, G, p, total, st);
+        launch_residue_epi(dt, vec, G, p, total, st, coop);
     } else {
-        launch_res_dt<false>(dt, vec, G, p, total, st);
+        launch_res_dt<false>(dt, vec, G, p, total, st, coop);
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "residue kernel launch");

@@ -31,6 +31,11 @@ struct Shard {
     int long_thr = 0;
     float *partials = nullptr;
     int pstride = 0;
+    // Packed {column, value bits} per nonzero, padded to a multiple of 16 entries,
+    // for the cooperative-chunk residue kernels (two or more lane groups per warp);
+    // null when the plan does not use them.
+    int2 *pairs = nullptr;
+    bool coop = false;
     unsigned int *counters = nullptr;
 
     // Tensor-core windows.
@@ -85,6 +90,7 @@ tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int6
 tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB, int64_t ldb, void *dC, int64_t ldc,
                               const Epilogue *ep, cudaStream_t st, const Int2 *ranges = nullptr, int n_ranges = 0);
 // The epilogue instantiations of the residue kernel (residue_epi.cu).
-void launch_residue_epi(tcaspmm_dtype dt, bool vec, int G, const ResidueParams &p, int total_warps, cudaStream_t st);
+void launch_residue_epi(tcaspmm_dtype dt, bool vec, int G, const ResidueParams &p, int total_warps, cudaStream_t st,
+                        bool coop);
 
 }  // namespace tca

@@ -3,9 +3,10 @@
 
 namespace tca {
 
-void launch_residue_epi(tcaspmm_dtype dt, bool vec, int G, const ResidueParams &p, int total_warps, cudaStream_t st)
+void launch_residue_epi(tcaspmm_dtype dt, bool vec, int G, const ResidueParams &p, int total_warps, cudaStream_t st,
+                        bool coop)
 {
-    launch_res_dt<true>(dt, vec, G, p, total_warps, st);
+    launch_res_dt<true>(dt, vec, G, p, total_warps, st, coop);
 }
 
 }  // namespace tca

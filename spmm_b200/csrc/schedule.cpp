@@ -36,7 +36,7 @@ void residue_shape(int64_t ncols, tcaspmm_dtype dt, bool vector_path, int *G, in
 
 // Integer tuning variable, clamped to [lo, hi]; unset, empty or not a whole
 // number (trailing characters included) gives the default.
-static int64_t env_int(const char *name, int64_t dflt, int64_t lo, int64_t hi)
+int64_t env_int(const char *name, int64_t dflt, int64_t lo, int64_t hi)
 {
     const char *s = std::getenv(name);
     if (!s || !*s) return dflt;
