@@ -98,6 +98,8 @@ typedef struct tcaspmm_plan_stats {
     double upload_ms;         /* plan upload (alloc + H2D) time */
     int64_t device_bytes;     /* device memory held by shard 0 */
     int64_t algorithmic_bytes;/* A + B + C bytes (A: (M+1)*4 + nnz*(4+sizeof(val))) */
+    int64_t tc_gathered_windows; /* tc windows of long rows grouped by length (row lists) */
+    int64_t tc_tasks;         /* tensor-core work items per column block (windows split by tiles) */
 } tcaspmm_plan_stats;
 
 /* ---------------------------------------------------------------- errors */
@@ -188,8 +190,11 @@ tcaspmm_status tcaspmm_partition_rows(const tcaspmm_csr *A, int parts, int64_t *
  *                              the groups otherwise, halved from eight groups)
  *   TCASPMM_BUDGET_MIN=128     floor on a lane group's nonzeros
  *   TCASPMM_WARPS_PER_SM=32    residue warps per SM the work is spread over
+ *   TCASPMM_HUB_WINDOWS=1      0: no gathered tensor-core windows of long rows
+ *   TCASPMM_SPLIT_TILES=128    tiles per work item of a gathered window
  * Values are clamped (BUDGET_MAX to [16, 2^20], BUDGET_MIN to [1, 2^20],
- * WARPS_PER_SM to [1, 1024], DISABLE_TC to [0, 1]); a value that is not a whole
+ * WARPS_PER_SM to [1, 1024], DISABLE_TC and HUB_WINDOWS to [0, 1], SPLIT_TILES
+ * to [1, 4096]); a value that is not a whole
  * number falls back to the default.  The results stay within the same
  * tolerances whatever these are; long rows may be summed in a different order. */
 

@@ -65,19 +65,24 @@ tcaspmm_status csr_from_rows(int64_t nrow, int64_t ncol, const std::vector<int64
 struct Int2 { int32_t x, y; };
 struct Int4 { int32_t x, y, z, w; };
 
-// Tensor-core window tiles.  A window is `R` consecutive rows; its condensed
-// columns are split into tiles of KT columns.  For tile t of window w:
-//   tile_cols[t * KT + k]       B row index of condensed column k (padding
-//                               columns repeat a valid index with zero values)
-//   tile_vals[t * R * KT + ...] the R x KT value block, row-major (row r, k)
-// windows[w] = {first row, first tile, number of tiles, rows in window}.
+// Tensor-core window tiles.  A window is up to `R` rows -- consecutive rows, or
+// a gathered list of long rows grouped by length -- whose condensed columns (the
+// sorted union of the rows' columns) are split into tiles of KT columns.  For
+// tile t of window w, tile_cols[t * KT + k] is the B row index of condensed
+// column k (padding columns repeat the last index and get zero values); the
+// R x KT value tile (row i of the window, k) is built from A at upload.
+// windows[w] = {x, first tile, number of tiles, rows in window}: x >= 0 is the
+// first of consecutive rows; x < 0 means rows[-(x + 1) + i] is the window's row i.
 struct TileSchedule {
     int R = 0;
     int KT = 0;
     std::vector<Int4> windows;
+    std::vector<int32_t> rows;     // row lists of the gathered windows
     std::vector<int32_t> tile_cols;
-    std::vector<float> tile_vals;  // widened; rounded to the device dtype at upload
     int64_t nnz = 0;
+    int64_t gathered = 0;          // gathered windows among `windows`
+    // Row i of window w.
+    int32_t row(const Int4 &w, int i) const { return w.x >= 0 ? w.x + i : rows[(size_t)(-(w.x + 1)) + i]; }
 };
 
 // CUDA-core residue work.  Row ranges are runs of rows that are neither in
@@ -98,8 +103,7 @@ struct Schedule {
     int64_t M = 0, K = 0, nnz = 0, ncols = 0;
     tcaspmm_dtype dt = TCASPMM_F32;
     TileSchedule tc;
-    std::vector<uint8_t> win_tc;  // per window of tc.R rows: 1 = tensor-core window
-    int win_shift = 4;
+    std::vector<uint8_t> row_tc;  // per row: 1 = in a tensor-core window
     ResidueSchedule res;
     double build_ms = 0.0;
 };

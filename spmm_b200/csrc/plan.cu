@@ -133,30 +133,6 @@ tcaspmm_status build_shard(const tcaspmm_csr &Afull, tcaspmm_dtype dt, int devic
             sh->val = d;
         }
     }
-    // Packed {column, value} pairs for the cooperative-chunk kernels, which run
-    // when a warp holds two or more lane groups (narrow column blocks); the
-    // value is the dtype-rounded value widened to fp32 (exact).
-    {
-        int G = 32, VEC = 4;
-        residue_shape(ncols, dt, true, &G, &VEC);
-        sh->coop = G >= 4 && G < 32 && ncols > 0 && A.nnz > 0 && env_flag("TCASPMM_RESIDUE_COOP", true);
-    }
-    if (sh->coop) {
-        const int64_t np = (A.nnz + 15) / 16 * 16 + 16;
-        std::vector<int2> pr((size_t)np, make_int2(0, 0));
-        std::vector<uint16_t> h16;
-        if (!dtype_fp32(dt) && A.val) h16 = to_16bit(A.val, A.nnz, dt);
-#pragma omp parallel for schedule(static)
-        for (int64_t j = 0; j < A.nnz; j++) {
-            float v = A.val ? A.val[j] : 1.0f;
-            if (!h16.empty())
-                v = dt == TCASPMM_F16 ? half_bits_to_float(h16[j]) : bf16_bits_to_float(h16[j]);
-            int vb;
-            std::memcpy(&vb, &v, 4);
-            pr[j] = make_int2(A.col_idx[j], vb);
-        }
-        if ((s = upload(*sh, &sh->pairs, pr.data(), pr.size(), "column/value pairs")) != TCASPMM_OK) return s;
-    }
     // Residue schedule and its scratch (partials + counters).
     const ResidueSchedule &RS = S.res;
     static_assert(sizeof(Int2) == sizeof(int2) && sizeof(Int4) == sizeof(int4), "layout");
@@ -223,19 +199,15 @@ tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB,
     p.segs = (const int4 *)sh.segs;
     p.n_segs = n_segs;
     p.longs = (const int4 *)sh.longs;
-    p.pairs = sh.pairs;
     p.partials = sh.partials;
     p.pstride = sh.pstride;
     p.counters = sh.counters;
     p.ep = EpiParams{nullptr, nullptr, 0, 0};
-    // Cooperative chunks need the pairs and the vector shape they were built for
-    // (the epilogue instantiations never take them).
-    const bool coop = sh.coop && vec && G >= 4 && G < 32 && !ep;
     if (ep) {
         p.ep = EpiParams{ep->row_scale, ep->bias, ep->relu, ep->out};
-        launch_residue_epi(dt, vec, G, p, total, st, coop);
+        launch_residue_epi(dt, vec, G, p, total, st);
     } else {
-        launch_res_dt<false>(dt, vec, G, p, total, st, coop);
+        launch_res_dt<false>(dt, vec, G, p, total, st);
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "residue kernel launch");
@@ -302,6 +274,8 @@ static tcaspmm_status create_common(const tcaspmm_csr *A, int64_t N, tcaspmm_dty
         if (split_rows ? P->shards[i]->col_begin != 0 : i != 0) continue;
         const Schedule &Si = P->shards[i]->sched;
         st.tc_windows += (int64_t)Si.tc.windows.size();
+        st.tc_gathered_windows += Si.tc.gathered;
+        st.tc_tasks += P->shards[i]->n_tasks;
         st.tc_tiles += Si.tc.KT ? (int64_t)Si.tc.tile_cols.size() / Si.tc.KT : 0;
         st.tc_nnz += Si.tc.nnz;
         st.residue_nnz += Si.res.nnz;
@@ -565,6 +539,11 @@ tcaspmm_status tcaspmm_plan_sync_check(tcaspmm_plan *plan)
         if (e != cudaSuccess) return cuda_fail(e, "read error word");
         if (err != 0) {
             cudaMemset(sh.err, 0, sizeof(int));
+            // An aborted launch may have left split windows part-counted: start
+            // the next launch from zero.
+            if (sh.tc_counters)
+                cudaMemset(sh.tc_counters, 0,
+                           sizeof(unsigned int) * (size_t)sh.n_split_groups * ((sh.ncols + 127) / 128) * 4);
             return fail(TCASPMM_ERR_TIMEOUT, "device %d: tensor-core kernel gave up waiting (code 0x%x)", sh.device, err);
         }
     }

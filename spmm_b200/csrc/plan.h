@@ -31,22 +31,24 @@ struct Shard {
     int long_thr = 0;
     float *partials = nullptr;
     int pstride = 0;
-    // Packed {column, value bits} per nonzero, padded to a multiple of 16 entries,
-    // for the cooperative-chunk residue kernels (two or more lane groups per warp);
-    // null when the plan does not use them.
-    int2 *pairs = nullptr;
-    bool coop = false;
     unsigned int *counters = nullptr;
 
-    // Tensor-core windows.
+    // Tensor-core windows and the tasks they are cut into.
     int n_windows = 0;
+    int n_tasks = 0;              // work items per column block
+    int n_split_groups = 0;       // gathered windows cut into several tasks
+    int n_fallback = 0;
     int num_sms = 148;
     int tc_ctas_per_sm = 1;       // resident tc-kernel CTAs per SM (persistent grid)
-    Int4 *tc_windows = nullptr;   // {first row, first tile, tiles, rows}, by decreasing tile count
-    int32_t *tc_dense = nullptr;  // per window: first column of its consecutive run, or -1
+    Int4 *tc_tasks = nullptr;     // {x, first tile, tiles, rows}, by decreasing tile count
+    Int4 *tc_splits = nullptr;    // per task {split window id or -1, part, parts, first partial slot}
+    int32_t *tc_rows = nullptr;   // row lists of the gathered windows
+    float *tc_partials = nullptr; // partial tiles of split windows (scratch)
+    unsigned int *tc_counters = nullptr;  // parts counted in per split window, zero between launches
+    int32_t *tc_dense = nullptr;  // per task: first column of its consecutive run, or -1
     int32_t *tc_cols = nullptr;   // KT B-row indices per tile
     void *tc_vals = nullptr;      // R x KT values per tile, shared-memory image
-    Int2 *tc_fallback = nullptr;  // one row range per window (unaligned B: CUDA cores)
+    Int2 *tc_fallback = nullptr;  // row ranges covering the tc rows (unaligned B: CUDA cores)
     // Tensor maps over the last B block launched (rebuilt when B or ldb change);
     // opaque storage for three 128-byte CUtensorMap objects.
     alignas(64) mutable unsigned char maps[384] = {};
@@ -90,7 +92,6 @@ tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int6
 tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB, int64_t ldb, void *dC, int64_t ldc,
                               const Epilogue *ep, cudaStream_t st, const Int2 *ranges = nullptr, int n_ranges = 0);
 // The epilogue instantiations of the residue kernel (residue_epi.cu).
-void launch_residue_epi(tcaspmm_dtype dt, bool vec, int G, const ResidueParams &p, int total_warps, cudaStream_t st,
-                        bool coop);
+void launch_residue_epi(tcaspmm_dtype dt, bool vec, int G, const ResidueParams &p, int total_warps, cudaStream_t st);
 
 }  // namespace tca

@@ -49,9 +49,6 @@ struct ResidueParams {
     const int4 *__restrict__ segs;   // {row, begin, end, long id}
     int n_segs;
     const int4 *__restrict__ longs;  // {row, first seg, number of segs, 0}
-    // Per nonzero {column, value as fp32 bits} (the COOP kernels); allocated to a
-    // multiple of 16 entries past nnz (zero-filled) so aligned chunk loads stay inside.
-    const int2 *__restrict__ pairs;
     float *partials;                 // n_segs x pstride
     int pstride;
     unsigned int *counters;          // one per long row, zero between launches
@@ -366,149 +363,6 @@ __device__ __forceinline__ void stream_lean(const ResidueParams &p, int r_lo, in
     }
 }
 
-// ---------------------------------------------------------------------------
-// Group-cooperative index loads (COOP kernels, two or more lane groups per warp).
-//
-// With G < 32 lanes per group, the P = 32 / G groups of a warp stream different
-// rows, so a per-lane load of a nonzero's column and of its value touches P
-// different cache lines per warp instruction: two L1 requests per nonzero on top
-// of the B row's one.  Here the G lanes of a group load the packed {column,
-// value} pairs of a chunk of U consecutive nonzeros together (one coalesced
-// 8-byte-per-pair load, U * 8 bytes per group) and each slot's pair reaches the
-// group's lanes by a shuffle, so the index stream costs U / G loads per lane
-// per U nonzeros.  Chunks start at multiples of U (so the group's load is one
-// aligned U * 8-byte block); slots outside the group's nonzero range are masked.
-
-// Pairs of chunk `base` held by lane gl of a G-lane group: with G <= U each lane
-// holds U / G consecutive pairs (16-byte loads), with G > U lanes 0..U-1 hold one.
-template <int G, int U> struct CoopChunk {
-    static constexpr int PPL = G <= U ? U / G : 1;  // pairs per lane
-    int2 pr[PPL];
-    __device__ __forceinline__ void load(const int2 *__restrict__ pairs, int base, int gl, int lo, int hi)
-    {
-        if constexpr (G <= U && PPL % 2 == 0) {
-            const int q = base + gl * PPL;  // multiple of 2: 16-byte aligned
-#pragma unroll
-            for (int k = 0; k < PPL; k += 2) {
-                if (q + k + 1 >= lo && q + k < hi) {
-                    const int4 x = __ldg(reinterpret_cast<const int4 *>(pairs + q + k));
-                    pr[k] = make_int2(x.x, x.y);
-                    pr[k + 1] = make_int2(x.z, x.w);
-                } else {
-                    pr[k] = pr[k + 1] = make_int2(0, 0);
-                }
-            }
-        } else {
-            const int q = base + gl;  // PPL == 1
-            pr[0] = (gl < U && q >= lo && q < hi) ? __ldg(pairs + q) : make_int2(0, 0);
-        }
-    }
-    // Slot u's column and value, from the lane that holds them (all G lanes of the
-    // group call these).
-    __device__ __forceinline__ int col(int u, unsigned gmask) const
-    {
-        return __shfl_sync(gmask, pr[u % PPL].x, u / PPL, G);
-    }
-    __device__ __forceinline__ float val(int u, unsigned gmask) const
-    {
-        return __int_as_float(__shfl_sync(gmask, pr[u % PPL].y, u / PPL, G));
-    }
-};
-
-// acc += sum_{j in [b, e)} val[j] * B[col[j]][c0 ..] through cooperative chunks;
-// every lane of the group calls this (colok false: the lane shuffles but loads no
-// B row).
-template <typename T, int VEC, int G, int U>
-__device__ __forceinline__ void accumulate_coop(const ResidueParams &p, const int b, const int e, int c0, bool colok,
-                                                unsigned gmask, float (&acc)[VEC])
-{
-    const char *Bb = reinterpret_cast<const char *>(static_cast<const T *>(p.B) + c0);
-    const unsigned pitch = (unsigned)(p.ldb * (long long)sizeof(T));
-    const int gl = (threadIdx.x & 31) % G;
-    for (int base = b & ~(U - 1); base < e; base += U) {
-        CoopChunk<G, U> ch;
-        ch.load(p.pairs, base, gl, b, e);
-        const bool full = base >= b && base + U <= e;
-        Raw<T, VEC> rb[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int c = ch.col(u, gmask);
-            if (colok && (full || (base + u >= b && base + u < e)))
-                load_raw<T, VEC>(brow<T>(Bb, c, pitch), rb[u]);
-            else
-                zero_raw<T, VEC>(rb[u]);
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) fma_raw<T, VEC>(ch.val(u, gmask), rb[u], acc);
-    }
-}
-
-// Lean stream over C rows [r_lo, r_hi) with cooperative chunks: as stream_lean,
-// but every lane of the group runs the loop (the group's lanes stay converged
-// for the shuffles), the next chunk's pairs are loaded while the current one's B
-// rows are in flight, and chunks inside one row skip the row-end checks.
-template <typename T, int VEC, int G, int U, bool EPI>
-__device__ __forceinline__ void stream_coop(const ResidueParams &p, int r_lo, int r_hi, int c0, bool colok,
-                                            unsigned gmask)
-{
-    if (r_lo >= r_hi) return;
-    const char *Bb = reinterpret_cast<const char *>(static_cast<const T *>(p.B) + c0);
-    const unsigned pitch = (unsigned)(p.ldb * (long long)sizeof(T));
-    const int gl = (threadIdx.x & 31) % G;
-    int r = r_lo;
-    int e = __ldg(p.row_ptr + r + 1);
-    int e_next = r + 1 < r_hi ? __ldg(p.row_ptr + r + 2) : 0;
-    const int jb = __ldg(p.row_ptr + r_lo);
-    const int jend = __ldg(p.row_ptr + r_hi);
-    EpiRegs<VEC, EPI> er;
-    if (colok) er.load_bias(p, c0);  // lanes past the last column have no bias
-    er.load_scale(p, r);
-    float acc[VEC];
-#pragma unroll
-    for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
-    auto flush_row = [&]() {
-        if (colok) emit<VEC, EPI>(p, r, c0, acc, er);
-#pragma unroll
-        for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
-        ++r;
-        e = e_next;
-        if (r + 1 < r_hi) e_next = __ldg(p.row_ptr + r + 2);
-        if (r < r_hi) er.load_scale(p, r);
-    };
-    int base = jb & ~(U - 1);
-    CoopChunk<G, U> ch, nx;
-    if (base < jend) ch.load(p.pairs, base, gl, jb, jend);
-    for (; base < jend; base += U) {
-        const bool full = base >= jb && base + U <= jend;
-        Raw<T, VEC> rb[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int c = ch.col(u, gmask);
-            if (colok && (full || (base + u >= jb && base + u < jend)))
-                load_raw<T, VEC>(brow<T>(Bb, c, pitch), rb[u]);
-            else
-                zero_raw<T, VEC>(rb[u]);
-        }
-        if (base + U < jend) nx.load(p.pairs, base + U, gl, jb, jend);  // next chunk, one step ahead
-        if (full && base + U <= e) {  // the whole chunk lies in the current row
-#pragma unroll
-            for (int u = 0; u < U; ++u) fma_raw<T, VEC>(ch.val(u, gmask), rb[u], acc);
-        } else {
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int j = base + u;
-                const float v = ch.val(u, gmask);  // every lane of the group shuffles
-                if (j >= jb && j < jend) {
-                    while (j >= e) flush_row();  // r < r_hi: nonzero j lies in a later row
-                    fma_raw<T, VEC>(v, rb[u], acc);
-                }
-            }
-        }
-        ch = nx;
-    }
-    while (r < r_hi) flush_row();  // the last row and trailing empty rows
-}
-
 // First row r in [lo, hi] with row_ptr[r] >= target.
 __device__ __forceinline__ int first_row_at(const int32_t *row_ptr, int lo, int hi, int target)
 {
@@ -526,18 +380,15 @@ __device__ __forceinline__ int first_row_at(const int32_t *row_ptr, int lo, int 
 // measured faster than 40 registers / 48 warps and than 80 / 24 on GCN, SAGE
 // and the skew config, the epilogue instantiations included (at 80 registers
 // they ran 25% slower on GCN for the lost occupancy).
-template <typename T, int VEC, int G, int U, bool EPI, bool PF = false, int BLOCK = 256, bool COOP = false>
+template <typename T, int VEC, int G, int U, bool EPI, bool PF = false, int BLOCK = 256>
 __global__ void __launch_bounds__(BLOCK, 1024 / BLOCK) residue_kernel(const ResidueParams p)
 {
     constexpr int P = 32 / G;
     constexpr int CPP = G * VEC;  // columns per pass
-    static_assert(!COOP || (G < 32 && (U & (U - 1)) == 0), "cooperative chunks: several groups, U a power of two");
     const int lane = threadIdx.x & 31;
     const int warp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
     const int sub = lane / G, gl = lane % G;
     const int npass = (p.ncols + CPP - 1) / CPP;
-    // The lanes of this lane group (shuffle mask of the cooperative chunks).
-    const unsigned gmask = G == 32 ? 0xffffffffu : ((1u << G) - 1u) << (sub * G);
 
     if (warp < p.n_segs) {
         const int4 s = p.segs[warp];
@@ -551,10 +402,7 @@ __global__ void __launch_bounds__(BLOCK, 1024 / BLOCK) residue_kernel(const Resi
             float acc[VEC];
 #pragma unroll
             for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
-            if constexpr (COOP)
-                accumulate_coop<T, VEC, G, U>(p, jb, je, c0, c0 < p.ncols, gmask, acc);
-            else if (c0 < p.ncols)
-                accumulate_lean<T, VEC, U, PF>(p, jb, je, c0, acc);
+            if (c0 < p.ncols) accumulate_lean<T, VEC, U, PF>(p, jb, je, c0, acc);
 #pragma unroll
             for (int off = G; off < 32; off <<= 1)
 #pragma unroll
@@ -613,12 +461,8 @@ __global__ void __launch_bounds__(BLOCK, 1024 / BLOCK) residue_kernel(const Resi
     }
     for (int pass = 0; pass < npass; ++pass) {
         const int c0 = pass * CPP + gl * VEC;
-        if constexpr (COOP) {
-            stream_coop<T, VEC, G, U, EPI>(p, r_lo, r_hi, c0, c0 < p.ncols, gmask);
-        } else {
-            if (c0 >= p.ncols) break;
-            stream_lean<T, VEC, U, EPI, PF>(p, r_lo, r_hi, c0);
-        }
+        if (c0 >= p.ncols) break;
+        stream_lean<T, VEC, U, EPI, PF>(p, r_lo, r_hi, c0);
     }
 }
 

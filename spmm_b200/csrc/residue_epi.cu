@@ -3,10 +3,9 @@
 
 namespace tca {
 
-void launch_residue_epi(tcaspmm_dtype dt, bool vec, int G, const ResidueParams &p, int total_warps, cudaStream_t st,
-                        bool coop)
+void launch_residue_epi(tcaspmm_dtype dt, bool vec, int G, const ResidueParams &p, int total_warps, cudaStream_t st)
 {
-    launch_res_dt<true>(dt, vec, G, p, total_warps, st, coop);
+    launch_res_dt<true>(dt, vec, G, p, total_warps, st);
 }
 
 }  // namespace tca

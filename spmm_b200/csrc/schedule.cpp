@@ -20,6 +20,8 @@
 #include <cstdlib>
 #include <cstring>
 
+#include <omp.h>
+
 #include "internal.h"
 
 namespace tca {
@@ -46,30 +48,56 @@ int64_t env_int(const char *name, int64_t dflt, int64_t lo, int64_t hi)
     return std::min<int64_t>(std::max<int64_t>(v, lo), hi);
 }
 
-// Condensed-tile selection for one window: returns the sorted union of the
-// window's columns and whether tiles beat per-nonzero gathers on bytes moved.
-static bool window_prefers_tc(const tcaspmm_csr &A, int64_t r0, int64_t r1, int KT, int R,
-                              int64_t ncols, int elem, std::vector<int32_t> *cols_u, int64_t *nnz_w)
+// The sorted union of the columns of `rows` (n of them) and their nonzero
+// count.  `marks` is a zeroed byte per column of A, left zeroed on return.
+static void column_union(const tcaspmm_csr &A, const int32_t *rows, int n, std::vector<uint8_t> &marks,
+                         std::vector<int32_t> *cols_u, int64_t *nnz_w)
 {
     cols_u->clear();
     int64_t nz = 0;
-    for (int64_t r = r0; r < r1; r++) {
-        const int64_t b = A.row_ptr[r], e = A.row_ptr[r + 1];
+    for (int i = 0; i < n; i++) {
+        const int64_t b = A.row_ptr[rows[i]], e = A.row_ptr[rows[i] + 1];
         nz += e - b;
-        cols_u->insert(cols_u->end(), A.col_idx + b, A.col_idx + e);
+        for (int64_t j = b; j < e; j++) {
+            const int32_t c = A.col_idx[j];
+            if (!marks[c]) {
+                marks[c] = 1;
+                cols_u->push_back(c);
+            }
+        }
     }
+    for (int32_t c : *cols_u) marks[c] = 0;
     *nnz_w = nz;
-    if (nz == 0) return false;
     std::sort(cols_u->begin(), cols_u->end());
-    cols_u->erase(std::unique(cols_u->begin(), cols_u->end()), cols_u->end());
-    const int64_t ntiles = ((int64_t)cols_u->size() + KT - 1) / KT;
+}
+
+// Bytes moved by a window of `nrows` rows as condensed tiles (16 gathered B rows
+// and an R x KT value tile per tile) against per-nonzero gathers on the CUDA cores.
+static bool tiles_pay(int64_t ucols, int64_t nz, int KT, int R, int64_t ncols, int elem)
+{
+    if (nz == 0) return false;
+    const int64_t ntiles = (ucols + KT - 1) / KT;
     const double row_bytes = (double)ncols * elem;
     const double tc_bytes = (double)ntiles * KT * (row_bytes + 4) + (double)ntiles * R * KT * elem;
     const double res_bytes = (double)nz * (row_bytes + 4 + elem);
-    const double density = (double)nz / ((double)ntiles * KT * (r1 - r0));
-    // A window is one serial chain of tiles on one CTA: cap its length so a hub
-    // window never becomes the critical path, and require real density.
-    return ntiles <= 256 && density >= 1.0 / 8.0 && tc_bytes < 0.8 * res_bytes;
+    return tc_bytes < 0.8 * res_bytes;
+}
+
+// Appends a window over rows[0..n) (x as in TileSchedule::windows) whose
+// condensed columns are cols_u, and marks its rows as tensor-core rows.
+static void add_window(const int32_t *rows, int n, int32_t x, const std::vector<int32_t> &cols_u, int64_t nz,
+                       Schedule *S)
+{
+    TileSchedule &T = S->tc;
+    const int KT = T.KT;
+    const int64_t ntiles = ((int64_t)cols_u.size() + KT - 1) / KT;
+    const int64_t t_first = (int64_t)T.tile_cols.size() / KT;
+    T.windows.push_back(Int4{x, (int32_t)t_first, (int32_t)ntiles, (int32_t)n});
+    const size_t cbase = T.tile_cols.size();
+    T.tile_cols.resize(cbase + ntiles * KT);
+    for (int64_t q = 0; q < ntiles * KT; q++) T.tile_cols[cbase + q] = q < (int64_t)cols_u.size() ? cols_u[q] : cols_u.back();
+    for (int i = 0; i < n; i++) S->row_tc[rows[i]] = 1;
+    T.nnz += nz;
 }
 
 tcaspmm_status build_schedule(const tcaspmm_csr &A, int64_t ncols, tcaspmm_dtype dt,
@@ -86,40 +114,87 @@ tcaspmm_status build_schedule(const tcaspmm_csr &A, int64_t ncols, tcaspmm_dtype
     const int elem = dtype_size(dt);
     const int64_t M = A.nrow;
 
-    // ---- tensor-core windows (16-bit dtypes) ----
+    // ---- tensor-core windows (16-bit dtypes and TF32) ----
     const int R = 32;
     S.tc.R = R;
     S.tc.KT = 16;
-    S.win_shift = 5;
-    const int64_t nwin = (M + R - 1) / R;
-    S.win_tc.assign((size_t)nwin, 0);
+    S.row_tc.assign((size_t)M, 0);
     const bool tc_ok = opt.allow_tc && dt != TCASPMM_F32 && ncols > 0 && ncols % 8 == 0 &&
                        env_int("TCASPMM_DISABLE_TC", 0, 0, 1) == 0;
     if (tc_ok) {
-        std::vector<int32_t> cols_u;
+        const int nth = omp_get_max_threads();
+        std::vector<std::vector<uint8_t>> marks(nth, std::vector<uint8_t>((size_t)A.ncol, 0));
+        // (1) Consecutive windows: blocks of R rows whose condensed tiles move fewer
+        // bytes, are at least 1/8 dense and have at most 256 tiles (one CTA runs a
+        // window's whole tile chain).  Evaluated in parallel, appended in order.
+        const int64_t nwin = (M + R - 1) / R;
+        std::vector<std::vector<int32_t>> ok_cols((size_t)nwin);
+        std::vector<int64_t> ok_nz((size_t)nwin, -1);
+#pragma omp parallel for schedule(dynamic, 64)
         for (int64_t w = 0; w < nwin; w++) {
-            const int64_t r0 = w * R, r1 = std::min<int64_t>(M, r0 + R);
+            const int64_t r0 = w * R;
+            const int n = (int)std::min<int64_t>(R, M - r0);
+            int32_t rows[32];
+            for (int i = 0; i < n; i++) rows[i] = (int32_t)(r0 + i);
+            std::vector<int32_t> cols_u;
             int64_t nz;
-            if (!window_prefers_tc(A, r0, r1, S.tc.KT, R, ncols, elem, &cols_u, &nz)) continue;
-            S.win_tc[w] = 1;
-            const int KT = S.tc.KT;
-            const int64_t ntiles = ((int64_t)cols_u.size() + KT - 1) / KT;
-            const int64_t t_first = (int64_t)S.tc.tile_cols.size() / KT;
-            S.tc.windows.push_back(Int4{(int32_t)r0, (int32_t)t_first, (int32_t)ntiles, (int32_t)(r1 - r0)});
-            const size_t cbase = S.tc.tile_cols.size();
-            S.tc.tile_cols.resize(cbase + ntiles * KT);
-            for (int64_t q = 0; q < ntiles * KT; q++)
-                S.tc.tile_cols[cbase + q] = q < (int64_t)cols_u.size() ? cols_u[q] : cols_u.back();
-            const size_t vbase = S.tc.tile_vals.size();
-            S.tc.tile_vals.resize(vbase + ntiles * R * KT, 0.0f);
-            for (int64_t r = r0; r < r1; r++) {
-                for (int64_t j = A.row_ptr[r]; j < A.row_ptr[r + 1]; j++) {
-                    const int64_t p = std::lower_bound(cols_u.begin(), cols_u.end(), A.col_idx[j]) - cols_u.begin();
-                    const int64_t t = p / KT, k = p % KT;
-                    S.tc.tile_vals[vbase + (t * R + (r - r0)) * KT + k] = A.val ? A.val[j] : 1.0f;
+            column_union(A, rows, n, marks[omp_get_thread_num()], &cols_u, &nz);
+            const int64_t ntiles = ((int64_t)cols_u.size() + S.tc.KT - 1) / S.tc.KT;
+            if (nz == 0 || ntiles > 256 || (double)nz < (double)ntiles * S.tc.KT * n / 8.0 ||
+                !tiles_pay((int64_t)cols_u.size(), nz, S.tc.KT, R, ncols, elem))
+                continue;
+            ok_cols[w] = std::move(cols_u);
+            ok_nz[w] = nz;
+        }
+        for (int64_t w = 0; w < nwin; w++) {
+            if (ok_nz[w] < 0) continue;
+            const int n = (int)std::min<int64_t>(R, M - w * R);
+            int32_t rows[32];
+            for (int i = 0; i < n; i++) rows[i] = (int32_t)(w * R + i);
+            add_window(rows, n, (int32_t)(w * R), ok_cols[w], ok_nz[w], &S);
+            std::vector<int32_t>().swap(ok_cols[w]);
+        }
+        // (2) Gathered windows of long rows: the remaining rows of at least
+        // 2 * KT nonzeros, longest first, taken R at a time while their condensed
+        // tiles pay (hub rows share their hub columns, so the union is smaller
+        // than the nonzero count); shorter rows pay less, so the first window that
+        // does not pay ends the search.  Their tile chains are split across CTAs
+        // at upload, so there is no tile cap.  Windows are evaluated in parallel
+        // batches and appended in order.
+        if (env_flag("TCASPMM_HUB_WINDOWS", true)) {
+            std::vector<int32_t> cand;
+            for (int64_t r = 0; r < M; r++)
+                if (!S.row_tc[r] && A.row_ptr[r + 1] - A.row_ptr[r] >= 2 * S.tc.KT) cand.push_back((int32_t)r);
+            std::stable_sort(cand.begin(), cand.end(), [&](int32_t a, int32_t b) {
+                return A.row_ptr[a + 1] - A.row_ptr[a] > A.row_ptr[b + 1] - A.row_ptr[b];
+            });
+            const int64_t ncw = ((int64_t)cand.size() + R - 1) / R;
+            bool stop = false;
+            for (int64_t b0 = 0; b0 < ncw && !stop; b0 += 2 * nth) {
+                const int64_t b1 = std::min<int64_t>(ncw, b0 + 2 * nth);
+                std::vector<std::vector<int32_t>> cu((size_t)(b1 - b0));
+                std::vector<int64_t> nzs((size_t)(b1 - b0));
+                std::vector<char> pays((size_t)(b1 - b0));
+#pragma omp parallel for schedule(dynamic, 1)
+                for (int64_t w = b0; w < b1; w++) {
+                    const int64_t c0 = w * R;
+                    const int n = (int)std::min<int64_t>(R, (int64_t)cand.size() - c0);
+                    column_union(A, cand.data() + c0, n, marks[omp_get_thread_num()], &cu[w - b0], &nzs[w - b0]);
+                    pays[w - b0] = tiles_pay((int64_t)cu[w - b0].size(), nzs[w - b0], S.tc.KT, R, ncols, elem);
+                }
+                for (int64_t w = b0; w < b1; w++) {
+                    if (!pays[w - b0]) {
+                        stop = true;
+                        break;
+                    }
+                    const int64_t c0 = w * R;
+                    const int n = (int)std::min<int64_t>(R, (int64_t)cand.size() - c0);
+                    const int32_t x = -(int32_t)(S.tc.rows.size() + 1);
+                    S.tc.rows.insert(S.tc.rows.end(), cand.begin() + c0, cand.begin() + c0 + n);
+                    add_window(cand.data() + c0, n, x, cu[w - b0], nzs[w - b0], &S);
+                    S.tc.gathered++;
                 }
             }
-            S.tc.nnz += nz;
         }
     }
 
@@ -129,7 +204,7 @@ tcaspmm_status build_schedule(const tcaspmm_csr &A, int64_t ncols, tcaspmm_dtype
     RS.P = 32 / RS.G;
     const int P = RS.P;
     const int64_t BETA = 2;  // per-row cost (row_ptr read, C row write) in nonzero units
-    auto in_tc = [&](int64_t r) { return S.win_tc[r >> S.win_shift] != 0; };
+    auto in_tc = [&](int64_t r) { return S.row_tc[r] != 0; };
     int64_t W = 0;
     for (int64_t r = 0; r < M; r++)
         if (!in_tc(r)) W += (A.row_ptr[r + 1] - A.row_ptr[r]) + BETA;
@@ -210,36 +285,29 @@ extern "C" tcaspmm_status tcaspmm_schedule_coverage(const tcaspmm_csr *A, int64_
         cover[j]++;
         kind[j] = k;
     };
-    // Tile cells: locate every nonzero of a tc window in its tiles and check
-    // the stored column and value; then count nonzero cells (no extras).
+    // Tile cells: every nonzero of a tc window's rows must find its column in the
+    // window's condensed columns (its value tile is built from that position).
     const int R = S.tc.R, KT = S.tc.KT;
-    int64_t cells = 0;
     for (const Int4 &w : S.tc.windows) {
         const int32_t *tc = S.tc.tile_cols.data() + (int64_t)w.y * KT;
-        const float *tv = S.tc.tile_vals.data() + (int64_t)w.y * R * KT;
         const int64_t ncond = (int64_t)w.z * KT;
-        for (int64_t r = w.x; r < w.x + w.w; r++) {
+        for (int64_t q = 1; q < ncond; q++)
+            if (tc[q] < tc[q - 1]) return fail(TCASPMM_ERR_FORMAT, "window columns not ascending");
+        for (int i = 0; i < w.w; i++) {
+            const int64_t r = S.tc.row(w, i);
             for (int64_t j = A->row_ptr[r]; j < A->row_ptr[r + 1]; j++) {
                 const int32_t c = A->col_idx[j];
                 int64_t p = std::lower_bound(tc, tc + ncond, c) - tc;
                 if (p >= ncond || tc[p] != c) continue;  // not covered: reported by cover[j] == 0
-                const float v = tv[((p / KT) * R + (r - w.x)) * KT + p % KT];
-                if (v != (A->val ? A->val[j] : 1.0f)) continue;
                 mark(j, 3);
             }
         }
-        for (int64_t q = 0; q < (int64_t)w.z * R * KT; q++) cells += tv[q] != 0.0f;
     }
-    int64_t tc_val_nnz = 0;
-    for (int64_t j = 0; j < A->nnz; j++) tc_val_nnz += kind[j] == 3 && (A->val ? A->val[j] : 1.0f) != 0.0f;
-    if (cells != tc_val_nnz)
-        return fail(TCASPMM_ERR_FORMAT, "tiles hold %lld nonzero cells for %lld covered nonzeros",
-                    (long long)cells, (long long)tc_val_nnz);
     // Residue, walked exactly as the kernel walks it.
     const ResidueSchedule &RS = S.res;
     for (const Int2 &rg : RS.ranges) {
         for (int64_t r = rg.x; r < rg.y; r++) {
-            if (S.win_tc[r >> S.win_shift])
+            if (S.row_tc[r])
                 return fail(TCASPMM_ERR_FORMAT, "row range holds tensor-core row %lld", (long long)r);
             for (int64_t j = A->row_ptr[r]; j < A->row_ptr[r + 1]; j++) mark(j, 1);
         }
@@ -259,6 +327,7 @@ extern "C" tcaspmm_status tcaspmm_schedule_coverage(const tcaspmm_csr *A, int64_
         stats->num_shards = 1;
         stats->window_rows = R;
         stats->tc_windows = (int64_t)S.tc.windows.size();
+        stats->tc_gathered_windows = S.tc.gathered;
         stats->tc_tiles = (int64_t)S.tc.tile_cols.size() / (KT ? KT : 1);
         stats->tc_nnz = S.tc.nnz;
         stats->residue_nnz = RS.nnz;

@@ -32,6 +32,13 @@
 // memory by a coalesced warp load.  Two TMEM accumulators let the epilogue of
 // one unit overlap the MMAs of the next.
 //
+// Work items ("tasks") are windows or, for the gathered windows of long rows
+// (rows grouped by length, any row indices), consecutive parts of a window's
+// tile chain, so one hub window's thousands of tiles spread over many CTAs.  A
+// part's epilogue warps store their 32 x 32 partial tile to scratch and count it
+// in; the warp that completes the window's last part adds the parts in part
+// order (deterministic) and writes the C rows through the window's row list.
+//
 // Every mbarrier wait is bounded: on time-out the kernel records a code in the
 // plan's error word, stops issuing work, drains its copies and MMAs (bounded),
 // frees TMEM and returns; tcaspmm_plan_sync_check reports TCASPMM_ERR_TIMEOUT and
@@ -99,8 +106,12 @@ constexpr int EPI_THREADS = 128;
 constexpr unsigned long long WAIT_CYCLES = 4ull << 30;  // ~2 s at 2 GHz: no legitimate wait comes close
 
 struct TcParams {
-    const int4 *windows;     // {first row, first tile, tiles, rows}, by decreasing tile count
-    const int32_t *dense_c0; // per window: first column when its columns are one consecutive run, else -1
+    const int4 *tasks;       // {x, first tile, tiles, rows} (x as in TileSchedule::windows), by decreasing tiles
+    const int4 *splits;      // per task {split window id or -1, part, parts, first partial slot of the window}
+    const int32_t *rows;     // row lists of the gathered windows
+    float *partials;         // [slot][column block][epilogue warp][32 x 32] partial tiles of split windows
+    unsigned int *counters;  // [split window][column block][epilogue warp], zero between launches
+    const int32_t *dense_c0; // per task: first column when its columns are one consecutive run, else -1
     const int32_t *tile_cols;
     const uint8_t *tile_vals;  // per tile: the value tile's shared-memory image
     const void *B;
@@ -223,20 +234,27 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
 // are deterministic.
 __device__ __forceinline__ int stage_at(int k, int rot, int nst) { return k + rot < nst ? k + rot : k + rot - nst; }
 
-// Epilogue of one output column f of a window's rows [row0, row0 + rows), after
-// the row scales were applied: bias, ReLU, then fp32 / fp16 / bf16 stores (a
-// warp writes 32 consecutive columns of a row).
-__device__ __forceinline__ void epilogue_store(const TcParams &p, int row0, int rows, int f, const float (&v)[32])
+// Per-thread stores of one output column f of a task's rows: lane i holds
+// `rid`, the C row of the window's row i (row scales already applied).  Bias and
+// ReLU when the epilogue is on, then fp32 / fp16 / bf16 stores; a warp writes 32
+// consecutive columns of each row.  Every lane of the warp calls this (the row
+// ids are broadcast by shuffles); lanes past the last column store nothing.
+__device__ __forceinline__ void epilogue_rows(const TcParams &p, int rid, int rows, int f, const float (&v)[32])
 {
     const EpiParams &ep = p.ep;
-    const float b = ep.bias ? __ldg(ep.bias + f) : 0.0f;
+    const bool colok = f < p.ncols;
+    const float b = (p.has_ep && ep.bias && colok) ? __ldg(ep.bias + f) : 0.0f;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-        if (r < rows) {
-            float x = v[r] + b;
-            if (ep.relu) x = fmaxf(x, 0.0f);
-            const long long o = (long long)(row0 + r) * p.ldc + f;
-            if (ep.out == 0)
+        const long long row = __shfl_sync(0xffffffffu, rid, r);
+        if (r < rows && colok) {
+            float x = v[r];
+            if (p.has_ep) {
+                x += b;
+                if (ep.relu) x = fmaxf(x, 0.0f);
+            }
+            const long long o = row * p.ldc + f;
+            if (!p.has_ep || ep.out == 0)
                 __stcs(static_cast<float *>(p.C) + o, x);
             else if (ep.out == 1)
                 static_cast<__half *>(p.C)[o] = __float2half_rn(x);
@@ -337,7 +355,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int4 w_first = make_int4(0, 0, 0, 0);
     int c_first = -1;
     if (warp >= 5 && (int)blockIdx.x < p.n_units) {
-        w_first = p.windows[blockIdx.x / p.nfb];
+        w_first = p.tasks[blockIdx.x / p.nfb];
         c_first = p.dense_c0[blockIdx.x / p.nfb];
     }
 
@@ -386,9 +404,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             asm volatile("prefetch.tensormap [%0];" ::"l"(tm_64) : "memory");
         }
         for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
-            const int win = u / p.nfb;
+            const int win = u / p.nfb;  // task
             const bool first = u == (int)blockIdx.x;
-            const int4 w = first ? w_first : p.windows[win];
+            const int4 w = first ? w_first : p.tasks[win];
             const int c0 = first ? c_first : p.dense_c0[win];
             const int n0 = (u % p.nfb) * MB;
             const int nst = (w.z + G::TPS - 1) / G::TPS;  // stages of this unit (w.z >= 1)
@@ -495,7 +513,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t g = 0, i = 0;
             bool ok = true;
             for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x, ++i) {
-                const int4 w = p.windows[u / p.nfb];
+                const int4 w = p.tasks[u / p.nfb];
                 const uint32_t a = i & 1;
                 if (!wait_bounded(smem_u32(&acce[a]), ((i >> 1) & 1) ^ 1, abort_flag, p.err, 2, p.wait_cycles)) break;
                 tc_fence_after();
@@ -543,7 +561,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // ------------------------------ epilogue -------------------------------
         uint32_t i = 0;
         for (int u = blockIdx.x; u < p.n_units; u += gridDim.x, ++i) {
-            const int4 w = p.windows[u / p.nfb];
+            const int t = u / p.nfb, fb = u % p.nfb;
+            const int4 w = p.tasks[t];
             const uint32_t a = i & 1;
             if (!__all_sync(0xffffffffu,
                             wait_bounded(smem_u32(&accf[a]), (i >> 1) & 1, abort_flag, p.err, 4, p.wait_cycles)))
@@ -553,16 +572,43 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + a * R, v);
             tc_fence_before();
             mbar_arrive(smem_u32(&acce[a]));
+            const int4 sp = p.splits[t];
+            if (sp.x >= 0) {
+                // One part of a split window: publish this warp's 32 x 32 partial
+                // tile and count it in; the warp that completes the window's last
+                // part sums all parts in part order and writes C.
+                float *mine = p.partials + ((((long long)(sp.w + sp.y) * p.nfb + fb) * 4 + warp) << 10);
+#pragma unroll
+                for (int r = 0; r < R; ++r) __stcg(mine + r * 32 + lane, v[r]);
+                __threadfence();
+                __syncwarp();
+                unsigned int *cnt = p.counters + ((long long)sp.x * p.nfb + fb) * 4 + warp;
+                unsigned int prev = 0;
+                if (lane == 0) prev = atomicAdd(cnt, 1u);
+                prev = __shfl_sync(0xffffffffu, prev, 0);
+                if (prev + 1 != (unsigned int)sp.z) continue;
+                __threadfence();
+#pragma unroll
+                for (int r = 0; r < R; ++r) v[r] = 0.0f;
+                for (int q = 0; q < sp.z; ++q) {
+                    const float *part = p.partials + ((((long long)(sp.w + q) * p.nfb + fb) * 4 + warp) << 10);
+#pragma unroll
+                    for (int r = 0; r < R; ++r) v[r] += __ldcg(part + r * 32 + lane);
+                }
+                if (lane == 0) *cnt = 0u;  // ready for the next launch
+            }
+            // C row of the window's row `lane` (gathered windows read their row list).
+            const int rid = w.x >= 0 ? w.x + lane : (lane < w.w ? __ldg(p.rows + (-(w.x + 1)) + lane) : 0);
             if (p.has_ep && p.ep.row_scale) {
-                // One coalesced load of the window's row scales, then a broadcast
-                // per row (all lanes converged here).
-                const float sc = lane < w.w ? __ldg(p.ep.row_scale + w.x + lane) : 1.0f;
+                // One load of the window's row scales, then a broadcast per row
+                // (all lanes converged here).
+                const float sc = lane < w.w ? __ldg(p.ep.row_scale + rid) : 1.0f;
 #pragma unroll
                 for (int r = 0; r < R; ++r) v[r] *= __shfl_sync(0xffffffffu, sc, r);
             }
-            const int x = (u % p.nfb) * MB + warp * 32;  // this warp's first output column
+            const int x = fb * MB + warp * 32;  // this warp's first output column
             const int f = x + lane;
-            if (p.tma_store) {
+            if (p.tma_store && w.x >= 0) {
                 // Stage the warp's 32 x 32 tile in shared memory (row r at
                 // 32 r elements, conflict-free), then one bulk tensor store; the
                 // tensor map clips rows past the block's end and columns past N.
@@ -594,15 +640,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         bulk_commit();
                     }
                 }
-            } else if (f < p.ncols) {
-                if (!p.has_ep) {
-                    float *c = static_cast<float *>(p.C) + (long long)w.x * p.ldc + f;
-#pragma unroll
-                    for (int r = 0; r < R; ++r)
-                        if (r < w.w) __stcs(c + (long long)r * p.ldc, v[r]);
-                } else {
-                    epilogue_store(p, w.x, w.w, f, v);
-                }
+            } else if (x < p.ncols) {  // warp-uniform
+                epilogue_rows(p, rid, w.w, f, v);
             }
         }
         if (p.tma_store && lane == 0) bulk_wait_all();  // C is written before the CTA exits
@@ -735,26 +774,85 @@ bool tc_supported()
     return major == 10;
 }
 
-tcaspmm_status tc_upload(const tcaspmm_csr &, tcaspmm_dtype dt, Shard *sh)
+// Tiles per task of a gathered window: its tile chain is cut into parts of at
+// most this many tiles (about 32 pipeline stages), so a hub window's work spreads
+// over many CTAs while each part still amortises its epilogue.  The tuning
+// variable TCASPMM_SPLIT_TILES (clamped to [1, 4096]) overrides it.
+constexpr int SPLIT_TILES = 128;
+
+tcaspmm_status tc_upload(const tcaspmm_csr &A, tcaspmm_dtype dt, Shard *sh)
 {
     const TileSchedule &T = sh->sched.tc;
     sh->n_windows = (int)T.windows.size();
     if (sh->n_windows == 0) return TCASPMM_OK;
     if (T.R != R || T.KT != KT) return fail(TCASPMM_ERR_UNSUPPORTED, "tile shape %dx%d not built", T.R, T.KT);
-    // Windows by decreasing tile count, so the persistent grid balances.
-    // (Sorted on the host, so the kernel reads a unit's window with one load.)
-    std::vector<Int4> windows(T.windows);
-    std::stable_sort(windows.begin(), windows.end(), [](const Int4 &a, const Int4 &b) { return a.z > b.z; });
+    // Windows whose columns are one consecutive run (padding repeats the last
+    // column) need no index loads: their tiles are boxes of consecutive B rows.
+    // Only when K >= 64, so that the 64- and 16-row boxes are never clipped.
+    auto dense_run = [&](const Int4 &w) -> int32_t {
+        if (sh->K < 64) return -1;
+        const int32_t *c = T.tile_cols.data() + (size_t)w.y * KT;
+        const int64_t n = (int64_t)w.z * KT;
+        int64_t q = 1;
+        for (; q < n && c[q] == c[0] + q; q++) {
+        }
+        for (; q < n; q++)
+            if (c[q] != c[q - 1]) return -1;  // not padding
+        return c[0];
+    };
+    // Tasks: consecutive windows whole; gathered windows in parts of at most
+    // SPLIT_TILES tiles (a window of one part needs no reduction).
+    struct Task {
+        Int4 d, sp;
+        int32_t dense;
+    };
+    std::vector<Task> tasks;
+    int32_t groups = 0, slots = 0;
+    const int split = (int)env_int("TCASPMM_SPLIT_TILES", SPLIT_TILES, 1, 4096);
+    for (const Int4 &w : T.windows) {
+        const int parts = w.x >= 0 ? 1 : (w.z + split - 1) / split;
+        if (parts == 1) {
+            tasks.push_back(Task{w, Int4{-1, 0, 1, 0}, w.x >= 0 ? dense_run(w) : -1});
+            continue;
+        }
+        for (int q = 0; q < parts; q++) {
+            const int32_t t0 = (int32_t)((int64_t)w.z * q / parts), t1 = (int32_t)((int64_t)w.z * (q + 1) / parts);
+            tasks.push_back(Task{Int4{w.x, w.y + t0, t1 - t0, w.w}, Int4{groups, q, parts, slots}, -1});
+        }
+        groups++;
+        slots += parts;
+    }
+    // Tasks by decreasing tile count, so the persistent grid balances (sorted on
+    // the host, so the kernel reads a unit's task with one load).
+    std::stable_sort(tasks.begin(), tasks.end(), [](const Task &a, const Task &b) { return a.d.z > b.d.z; });
+    std::vector<Int4> td(tasks.size()), ts(tasks.size());
+    std::vector<int32_t> dense(tasks.size());
+    for (size_t i = 0; i < tasks.size(); i++) {
+        td[i] = tasks[i].d;
+        ts[i] = tasks[i].sp;
+        dense[i] = tasks[i].dense;
+    }
+    sh->n_tasks = (int)tasks.size();
+    sh->n_split_groups = groups;
     // Value tiles -> shared-memory image (K-major, no swizzle): core matrices of
     // 8 rows x 16 bytes, 16-byte k chunks 128 B apart (LBO), 8-row groups
     // kch * 128 B apart (SBO); fp16 / bf16 bits, or fp32 bits for tf32.
+    // Each nonzero of a window's row i lands at (tile, k) = the position of its
+    // column among the window's condensed columns; every other cell is zero.
     const int es = dtype_size(dt), kch = KT * es / 16, tile_bytes = R * KT * es;
     const size_t ntiles = T.tile_cols.size() / KT;
-    std::vector<uint8_t> img(ntiles * tile_bytes);
-    for (size_t t = 0; t < ntiles; t++)
-        for (int n = 0; n < R; n++)
-            for (int k = 0; k < KT; k++) {
-                const float v = T.tile_vals[(t * R + n) * KT + k];
+    std::vector<uint8_t> img(ntiles * tile_bytes, 0);
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int64_t wi = 0; wi < (int64_t)T.windows.size(); wi++) {
+        const Int4 &w = T.windows[wi];
+        const int32_t *cols = T.tile_cols.data() + (size_t)w.y * KT;
+        const int64_t ncond = (int64_t)w.z * KT;
+        for (int n = 0; n < w.w; n++) {
+            const int64_t r = T.row(w, n);
+            for (int64_t j = A.row_ptr[r]; j < A.row_ptr[r + 1]; j++) {
+                const int64_t q = std::lower_bound(cols, cols + ncond, A.col_idx[j]) - cols;
+                const int64_t t = w.y + q / KT, k = q % KT;
+                const float v = A.val ? A.val[j] : 1.0f;
                 uint8_t *dst = img.data() + t * tile_bytes + (n / 8) * (kch * 128) + (k * es / 16) * 128 +
                                (n % 8) * 16 + (k * es) % 16;
                 if (es == 4) {
@@ -764,30 +862,45 @@ tcaspmm_status tc_upload(const tcaspmm_csr &, tcaspmm_dtype dt, Shard *sh)
                     std::memcpy(dst, &h, 2);
                 }
             }
-    // Windows whose columns are one consecutive run (padding repeats the last
-    // column) need no index loads: their tiles are boxes of consecutive B rows.
-    // Only when K >= 64, so that the 64- and 16-row boxes are never clipped.
-    std::vector<int32_t> dense(windows.size(), -1);
-    for (size_t i = 0; i < windows.size() && sh->K >= 64; i++) {
-        const int32_t *c = T.tile_cols.data() + (size_t)windows[i].y * KT;
-        const int64_t n = (int64_t)windows[i].z * KT;
-        bool ok = true;
-        int64_t q = 1;
-        for (; q < n && c[q] == c[0] + q; q++) {
         }
-        for (; q < n && ok; q++) ok = c[q] == c[q - 1];  // padding
-        if (ok) dense[i] = c[0];
     }
-    // Fallback row ranges over tc rows (run on the CUDA cores when B or C is
-    // not 16-byte aligned at execute time).
+    // Fallback row ranges over the tc rows (run on the CUDA cores when B is not
+    // 16-byte aligned at execute time): a consecutive window is one range, a
+    // gathered window one range per row.
     std::vector<Int2> fb;
-    for (const Int4 &w : T.windows) fb.push_back(Int2{w.x, w.x + w.w});
+    for (const Int4 &w : T.windows) {
+        if (w.x >= 0) {
+            fb.push_back(Int2{w.x, w.x + w.w});
+        } else {
+            for (int i = 0; i < w.w; i++) fb.push_back(Int2{T.row(w, i), T.row(w, i) + 1});
+        }
+    }
+    sh->n_fallback = (int)fb.size();
+    const int64_t nfb = (sh->ncols + MB - 1) / MB;
     tcaspmm_status s;
-    if ((s = upload_vec(sh, &sh->tc_windows, windows, "tc windows")) != TCASPMM_OK) return s;
+    if ((s = upload_vec(sh, &sh->tc_tasks, td, "tc tasks")) != TCASPMM_OK) return s;
+    if ((s = upload_vec(sh, &sh->tc_splits, ts, "tc splits")) != TCASPMM_OK) return s;
     if ((s = upload_vec(sh, &sh->tc_dense, dense, "tc dense runs")) != TCASPMM_OK) return s;
+    if ((s = upload_vec(sh, &sh->tc_rows, T.rows, "tc row lists")) != TCASPMM_OK) return s;
     if ((s = upload_vec(sh, &sh->tc_cols, T.tile_cols, "tc columns")) != TCASPMM_OK) return s;
     if ((s = upload_vec(sh, (uint8_t **)&sh->tc_vals, img, "tc values")) != TCASPMM_OK) return s;
     if ((s = upload_vec(sh, &sh->tc_fallback, fb, "tc fallback ranges")) != TCASPMM_OK) return s;
+    if (slots > 0) {
+        // Partial tiles: [slot][column block][4 epilogue warps][32 x 32] fp32, and
+        // one counter per (split window, column block, epilogue warp).
+        if ((s = upload_vec(sh, &sh->tc_counters, std::vector<unsigned int>((size_t)groups * nfb * 4, 0u),
+                            "tc split counters")) != TCASPMM_OK)
+            return s;
+        const size_t pbytes = (size_t)slots * nfb * 4 * 1024 * sizeof(float);
+        cudaError_t e = cudaMalloc((void **)&sh->tc_partials, pbytes);
+        if (e != cudaSuccess) {
+            sh->tc_partials = nullptr;
+            return fail(TCASPMM_ERR_ALLOC, "cudaMalloc of %zu bytes for tc partial tiles failed: %s", pbytes,
+                        cudaGetErrorString(e));
+        }
+        sh->allocs.push_back(sh->tc_partials);
+        sh->bytes += (int64_t)pbytes;
+    }
     int nsm = 148;
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, sh->device);
     sh->num_sms = nsm;
@@ -805,12 +918,16 @@ tcaspmm_status tc_upload(const tcaspmm_csr &, tcaspmm_dtype dt, Shard *sh)
 tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int64_t ldb, void *dC, int64_t ldc,
                          const Epilogue *ep, cudaStream_t st)
 {
-    if (sh.n_windows == 0 || sh.ncols == 0) return TCASPMM_OK;
+    if (sh.n_tasks == 0 || sh.ncols == 0) return TCASPMM_OK;
     const bool aligned = ((uintptr_t)dB % 16 == 0) && ((ldb * dtype_size(dt)) % 16 == 0) && (sh.ncols % 8 == 0);
     if (!aligned)  // CUDA-core fallback over the tc rows: whole rows, no segments
-        return launch_residue(sh, dt, dB, ldb, dC, ldc, ep, st, sh.tc_fallback, sh.n_windows);
+        return launch_residue(sh, dt, dB, ldb, dC, ldc, ep, st, sh.tc_fallback, sh.n_fallback);
     TcParams p;
-    p.windows = (const int4 *)sh.tc_windows;
+    p.tasks = (const int4 *)sh.tc_tasks;
+    p.splits = (const int4 *)sh.tc_splits;
+    p.rows = sh.tc_rows;
+    p.partials = sh.tc_partials;
+    p.counters = sh.tc_counters;
     p.dense_c0 = sh.tc_dense;
     p.tile_cols = sh.tc_cols;
     p.tile_vals = (const uint8_t *)sh.tc_vals;
@@ -820,7 +937,7 @@ tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int6
     p.ldc = ldc;
     p.ncols = (int)sh.ncols;
     p.nfb = (int)((sh.ncols + MB - 1) / MB);
-    p.n_units = sh.n_windows * p.nfb;
+    p.n_units = sh.n_tasks * p.nfb;
     p.err = sh.err;
     p.wait_cycles = WAIT_CYCLES;
     p.stall_test = 0;
@@ -871,16 +988,19 @@ extern "C" tcaspmm_status tcaspmm_selftest_tc_timeout(int device, unsigned long 
     if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
     if (!tc_supported()) return fail(TCASPMM_ERR_UNSUPPORTED, "device %d is not sm_100", device);
     const int4 win = make_int4(0, 0, 1, R);
+    const int4 nosplit = make_int4(-1, 0, 1, 0);
     const std::vector<int32_t> cols(KT, 0);
     const std::vector<uint16_t> vals(R * KT, 0);
     const int32_t no_run = -1;
-    void *d_win = nullptr, *d_dense = nullptr, *d_cols = nullptr, *d_vals = nullptr, *d_b = nullptr, *d_c = nullptr;
+    void *d_win = nullptr, *d_split = nullptr, *d_dense = nullptr, *d_cols = nullptr, *d_vals = nullptr,
+         *d_b = nullptr, *d_c = nullptr;
     int *d_err = nullptr;
     tcaspmm_status st = TCASPMM_OK;
     auto alloc = [&](void **ptr, size_t n) {
         if (st == TCASPMM_OK && (e = cudaMalloc(ptr, n)) != cudaSuccess) st = cuda_fail(e, "self-test allocation");
     };
     alloc(&d_win, sizeof(win));
+    alloc(&d_split, sizeof(nosplit));
     alloc(&d_dense, sizeof(no_run));
     alloc(&d_cols, cols.size() * 4);
     alloc(&d_vals, vals.size() * 2);
@@ -890,6 +1010,7 @@ extern "C" tcaspmm_status tcaspmm_selftest_tc_timeout(int device, unsigned long 
     BMaps maps;
     if (st == TCASPMM_OK) {
         cudaMemcpy(d_win, &win, sizeof(win), cudaMemcpyHostToDevice);
+        cudaMemcpy(d_split, &nosplit, sizeof(nosplit), cudaMemcpyHostToDevice);
         cudaMemcpy(d_dense, &no_run, sizeof(no_run), cudaMemcpyHostToDevice);
         cudaMemcpy(d_cols, cols.data(), cols.size() * 4, cudaMemcpyHostToDevice);
         cudaMemcpy(d_vals, vals.data(), vals.size() * 2, cudaMemcpyHostToDevice);
@@ -899,7 +1020,11 @@ extern "C" tcaspmm_status tcaspmm_selftest_tc_timeout(int device, unsigned long 
     }
     if (st == TCASPMM_OK) {
         TcParams p;
-        p.windows = (const int4 *)d_win;
+        p.tasks = (const int4 *)d_win;
+        p.splits = (const int4 *)d_split;
+        p.rows = nullptr;
+        p.partials = nullptr;
+        p.counters = nullptr;
         p.dense_c0 = (const int32_t *)d_dense;
         p.tile_cols = (const int32_t *)d_cols;
         p.tile_vals = (const uint8_t *)d_vals;
@@ -932,7 +1057,7 @@ extern "C" tcaspmm_status tcaspmm_selftest_tc_timeout(int device, unsigned long 
                      : fail(TCASPMM_OK, "no time-out recorded");
         }
     }
-    for (void *ptr : {d_win, d_dense, d_cols, d_vals, d_b, d_c, (void *)d_err})
+    for (void *ptr : {d_win, d_split, d_dense, d_cols, d_vals, d_b, d_c, (void *)d_err})
         if (ptr) cudaFree(ptr);
     return st;
 }

@@ -10,6 +10,7 @@
 """
 import json
 import os
+import re
 import subprocess
 
 import numpy as np
@@ -92,5 +93,7 @@ def test_reference_driver_linked_against_this_library(bundled_smtx_path):
     assert "validation failed" not in out, out
     for line in ("Input file - ", "GemmEx :", "cuSPARSE:", "our:", "preprocess "):
         assert line in out, out
-    ours = float(out.split("our:")[1].split("[")[1].split("]")[0])
-    assert ours > 0
+    # "our: \033[36m[<ms>] ms\033[0m": the timing sits between the colour codes.
+    m = re.search(r"our:\s*(?:\x1b\[[0-9;]*m)?\[([0-9.eE+-]+)\] ms", out)
+    assert m, out
+    assert float(m.group(1)) > 0

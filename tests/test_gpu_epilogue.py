@@ -134,3 +134,13 @@ def test_sage_mean_is_pattern_times_inverse_degree():
     got, _ = _run(pattern, B, "f32", scale=inv)
     mean = T.CSR(A.nrow, A.ncol, A.row_ptr, A.col, np.repeat(inv, np.diff(A.row_ptr)))
     assert oracle.rel_l2(got, oracle.spmm_f64(mean.row_ptr, mean.col, mean.values(), B)) <= 1e-5
+
+
+@pytest.mark.parametrize("out", ["f32", "bf16"])
+@pytest.mark.parametrize("split", ["128", "4"])
+def test_epilogue_through_gathered_windows(out, split, monkeypatch):
+    """Row scales, bias and ReLU applied through the row lists of the gathered windows of
+    long rows, with and without their tile chains split into parts."""
+    monkeypatch.setenv("TCASPMM_SPLIT_TILES", split)
+    st = _check(T.gen_rmat(15, 400000, kind="gcn", seed=2), 128, "f16", out, scale=_scale, bias=_bias, relu=True)
+    assert st["tc_gathered_windows"] > 0

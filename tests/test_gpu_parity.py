@@ -362,3 +362,59 @@ def test_tensor_core_stage_shapes_bit_exact():
             out, st = run(A, B[:, :N], dt)
             assert st["tc_windows"] == len(unions) and st["tc_nnz"] == st["nnz"], st
             np.testing.assert_array_equal(out, reference(A, B[:, :N], dt).astype(np.float32))
+
+
+# ---------------------------------------------------- gathered windows (long rows)
+@pytest.mark.parametrize("dt", ["f16", "bf16", "tf32"])
+@pytest.mark.parametrize("N", [128, 64, 256, 200])
+@pytest.mark.parametrize("split", ["128", "7"])
+def test_gathered_windows_of_long_rows(dt, N, split, monkeypatch):
+    """Long rows of a power-law graph grouped by length into tensor-core windows; their
+    tile chains cut into parts of `split` tiles (reduced in part order), C written
+    through the windows' row lists; N = 200 leaves a partial column block."""
+    monkeypatch.setenv("TCASPMM_SPLIT_TILES", split)
+    A = T.gen_rmat(15, 400000, kind="gcn", seed=2)
+    out, st = check(A, N, dt, seed=5)
+    assert st["tc_gathered_windows"] > 0 and st["tc_tasks"] > st["tc_windows"], st
+
+
+def test_gathered_windows_integer_values_bit_exact(monkeypatch):
+    """Integer A and B small enough that every fp32 sum is exact: tiles, split parts
+    and the fixed-order reduction must reproduce the oracle bit for bit."""
+    monkeypatch.setenv("TCASPMM_SPLIT_TILES", "5")
+    A = T.gen_rmat(13, 120000, kind="gcn", seed=9)
+    g = np.random.default_rng(9)
+    A = T.CSR(A.nrow, A.ncol, A.row_ptr, A.col, g.integers(-3, 4, A.nnz).astype(np.float32))
+    B = g.integers(-4, 5, (A.ncol, 128)).astype(np.float32)
+    out, st = run(A, B, "f16")
+    assert st["tc_gathered_windows"] > 0, st
+    np.testing.assert_array_equal(out, reference(A, B, "f16"))
+
+
+def test_gathered_windows_are_deterministic(monkeypatch):
+    monkeypatch.setenv("TCASPMM_SPLIT_TILES", "3")
+    A = T.gen_rmat(14, 200000, kind="gcn", seed=6)
+    B = T.gen_dense(A.ncol, 128, 2, "f32")
+    a, st = run(A, B, "bf16")
+    b, _ = run(A, B, "bf16")
+    assert st["tc_gathered_windows"] > 0
+    np.testing.assert_array_equal(a, b)
+
+
+def test_gathered_windows_with_unaligned_b_fall_back(monkeypatch):
+    A = T.gen_rmat(14, 200000, kind="gcn", seed=6)
+    B = T.gen_dense(A.ncol, 64, 2, "f32")
+    out, st = run(A, B, "f16", ldb_pad=3)  # ldb = 67 halves: rows not 16-byte aligned
+    assert st["tc_gathered_windows"] > 0
+    assert oracle.rel_l2(out, reference(A, B, "f16")) <= TOL_CORE
+
+
+def test_gathered_windows_switched_off_gives_the_same_product(monkeypatch):
+    A = T.gen_rmat(14, 200000, kind="gcn", seed=7)
+    B = T.gen_dense(A.ncol, 128, 4, "f32")
+    on, st_on = run(A, B, "f16")
+    monkeypatch.setenv("TCASPMM_HUB_WINDOWS", "0")
+    off, st_off = run(A, B, "f16")
+    assert st_on["tc_gathered_windows"] > 0 and st_off["tc_gathered_windows"] == 0
+    ref = reference(A, B, "f16")
+    assert oracle.rel_l2(on, ref) <= TOL_TC and oracle.rel_l2(off, ref) <= TOL_TC

@@ -307,3 +307,28 @@ def test_binary_csr_roundtrip(tmp_path):
         f.write(b"x")
     with pytest.raises(T.TcaspmmError):
         T.csrbin_read(p)
+
+
+@pytest.mark.parametrize("case,dt,N", [("gcn", "f16", 128), ("gcn", "bf16", 64), ("gcn", "tf32", 128),
+                                       ("sage", "f16", 256), ("skew", "f16", 64)])
+def test_gathered_windows_cover_long_rows_exactly_once(case, dt, N):
+    """Long rows grouped by length into tensor-core windows (row lists): every nonzero
+    is still covered exactly once, and the windows appear in the stats."""
+    if case == "gcn":
+        A = T.gen_rmat(15, 400000, kind="gcn", seed=2)
+    elif case == "sage":
+        A = T.gen_rmat(15, 400000, kind="sage", seed=3)
+    else:
+        A = T.gen_skew(100000, 16, 20000, 3.0, seed=4)
+    cover, kind, st = T.schedule_coverage(A, N, dt)
+    assert np.all(cover == 1), np.bincount(cover)
+    assert st["tc_gathered_windows"] > 0, st
+    assert st["tc_nnz"] + st["residue_nnz"] == A.nnz
+    assert (kind == 3).sum() == st["tc_nnz"]
+
+
+def test_gathered_windows_can_be_switched_off(monkeypatch):
+    A = T.gen_rmat(15, 400000, kind="gcn", seed=2)
+    monkeypatch.setenv("TCASPMM_HUB_WINDOWS", "0")
+    cover, _, st = T.schedule_coverage(A, 128, "f16")
+    assert np.all(cover == 1) and st["tc_gathered_windows"] == 0
