@@ -592,6 +592,14 @@ def main():
         Ad[rows, torch.from_numpy(A.col.astype(np.int64)).to(dev)] = torch.from_numpy(A.values()).to(dev).to(tdt)
         Cg = torch.empty_like(Cd)
         gemm = max_over_ranks(T.cublas_gemm(Ad, Bd, Cg, dt, warmup=3, iters=20, stream=stream))
+    # The per-nonzero gather floor: the same B-row gathers with no arithmetic and no C
+    # write, timed alone under the same L2 protocol (what any SpMM that gathers each
+    # nonzero's B row needs at least on this GPU).
+    try:
+        ms_gather = max_over_ranks(T.gather_floor(plan, Bd, warmup=3, iters=max(5, min(args.steps, 30)),
+                                                  stream=stream))
+    except Exception as e:  # reported
+        ms_gather = str(e)
     T.baselines_set_flush(None)
 
     # ---- CPU baseline (rank 0, N=1 only) ----
@@ -635,6 +643,12 @@ def main():
                          "frac": round(achieved / peak, 4), "traffic": load_traffic(args.workload),
                          "peak_kind": peak_kind, "algorithmic_bytes": alg,
                          "kernel": "residue_kernel" if pst["tc_windows"] == 0 else "tc + residue"},
+            "roofline_gather": {
+                "bound": "L2-to-SM gathers: every nonzero's B row slice, loaded alone (tcaspmm_gather_floor)",
+                "floor_ms": round(ms_gather, 5) if isinstance(ms_gather, float) else ms_gather,
+                "kernel_ms": round(ms_step, 5),
+                "frac": round(ms_gather / ms_step, 4) if isinstance(ms_gather, float) else None,
+                "gathered_bytes": int(pst["nnz"]) * ncols * elem if args.split == "columns" else None},
             "e2e": {"value": round(flops / (ms_e2e * 1e-3) / 1e9, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 4),
                     "pipeline": "copy-in, execute, copy-out on three streams, two device buffers"},

@@ -43,6 +43,16 @@ tcaspmm_status tcaspmm_cusparse_blocked_ell(const tcaspmm_csr *A, int block, con
                                            int64_t ldc, int64_t N, tcaspmm_dtype dt, int warmup, int iters,
                                            void *stream, double *ms_per_iter, int64_t *ell_bytes);
 
+/* Gather floor of a CSR SpMM (no counterpart in the reference; a measurement
+ * aid): loads every nonzero's B row slice (ncols elements of dt, ld ldb, 16-byte
+ * aligned rows) the way tcaspmm's CUDA-core kernel does -- 16 bytes per lane,
+ * several rows per warp instruction when ncols is narrow, 8 loads in flight --
+ * for the column indices d_col[0..nnz), with no arithmetic and no C write.  Its
+ * time is the floor any per-nonzero-gather SpMM of this matrix has on this GPU
+ * (the L2-to-SM gather rate), beside which the kernel's own time is reported. */
+tcaspmm_status tcaspmm_gather_floor(const int32_t *d_col, int64_t nnz, const void *dB, int64_t ldb, int64_t ncols,
+                                    tcaspmm_dtype dt, int warmup, int iters, void *stream, double *ms_per_iter);
+
 /* Device CSR arrays that a plan uploaded for `shard` (int32 offsets, int32
  * columns, values in the plan's dtype); lets a baseline run on the same bytes. */
 tcaspmm_status tcaspmm_plan_device_csr(const tcaspmm_plan *plan, int shard, const int32_t **row_ptr,

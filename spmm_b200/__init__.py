@@ -535,6 +535,9 @@ def baselines():
         _blib.tcaspmm_cusparse_blocked_ell.argtypes = [_P(_CSR), C.c_int, _vp, _i64, _vp, _i64, _i64, C.c_int,
                                                        C.c_int, C.c_int, _vp, _P(C.c_double), _P(_i64)]
         _blib.tcaspmm_cusparse_blocked_ell.restype = C.c_int
+        _blib.tcaspmm_gather_floor.argtypes = [_vp, _i64, _vp, _i64, _i64, C.c_int, C.c_int, C.c_int, _vp,
+                                               _P(C.c_double)]
+        _blib.tcaspmm_gather_floor.restype = C.c_int
         _blib.tcaspmm_baselines_set_flush.argtypes = [_vp, C.c_size_t]
         _blib.tcaspmm_baselines_set_flush.restype = None
     return _blib
@@ -569,6 +572,17 @@ def cusparse_spmm(plan: Plan, B, Cout, warmup: int = 10, iters: int = 10, stream
                                              int(B.stride(0)),
                                              _ptr(Cout), int(Cout.stride(0)), ncols, int(plan.dt), warmup, iters,
                                              _stream_handle(stream), C.byref(ms)))
+    return ms.value
+
+
+def gather_floor(plan: Plan, B, warmup: int = 3, iters: int = 10, stream=None, shard: int = 0) -> float:
+    """Time the per-nonzero B-row gathers of the plan's shard alone (no arithmetic, no C
+    write): the floor of a gather-per-nonzero SpMM on this GPU.  Returns ms per call."""
+    _, col, _ = plan.device_csr(shard)
+    _, _, ncols = plan.shard(shard)
+    ms = C.c_double()
+    _check(baselines().tcaspmm_gather_floor(col, plan.shard_nnz(shard), _ptr(B), int(B.stride(0)), ncols,
+                                            int(plan.dt), warmup, iters, _stream_handle(stream), C.byref(ms)))
     return ms.value
 
 

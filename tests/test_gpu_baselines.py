@@ -53,3 +53,14 @@ def test_cublas_gold_matches_the_oracle(dt):
     ms = T.cublas_gemm(Ad, Bd, C, dt, warmup=1, iters=2)
     assert ms > 0
     assert oracle.rel_l2(C.cpu().numpy(), ref) <= 1e-5
+
+
+@pytest.mark.parametrize("dt,N", [("f32", 128), ("f32", 16), ("f16", 64)])
+def test_gather_floor_runs_on_the_plan_columns(dt, N):
+    """The gather-floor measurement (reported beside the kernel's time) runs on the plan's
+    own device columns and B and takes positive time."""
+    tdt = {"f16": torch.float16, "f32": torch.float32}[dt]
+    A = T.gen_rmat(13, 80000, kind="gcn", seed=1)
+    Bd = torch.from_numpy(T.gen_dense(A.ncol, N, 1, "f32")).to(tdt).cuda()
+    with T.Plan(A, N, dt) as p:
+        assert T.gather_floor(p, Bd, warmup=1, iters=3) > 0
