@@ -190,7 +190,8 @@ tcaspmm_status tcaspmm_partition_rows(const tcaspmm_csr *A, int parts, int64_t *
  *                              the groups otherwise, halved from eight groups)
  *   TCASPMM_BUDGET_MIN=128     floor on a lane group's nonzeros
  *   TCASPMM_WARPS_PER_SM=32    residue warps per SM the work is spread over
- *   TCASPMM_HUB_WINDOWS=1      0: no gathered tensor-core windows of long rows
+ *   TCASPMM_HUB_WINDOWS=0      1: long rows grouped by length into gathered
+ *                              tensor-core windows
  *   TCASPMM_SPLIT_TILES=128    tiles per work item of a gathered window
  * Values are clamped (BUDGET_MAX to [16, 2^20], BUDGET_MIN to [1, 2^20],
  * WARPS_PER_SM to [1, 1024], DISABLE_TC and HUB_WINDOWS to [0, 1], SPLIT_TILES

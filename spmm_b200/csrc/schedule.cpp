@@ -161,7 +161,7 @@ tcaspmm_status build_schedule(const tcaspmm_csr &A, int64_t ncols, tcaspmm_dtype
         // does not pay ends the search.  Their tile chains are split across CTAs
         // at upload, so there is no tile cap.  Windows are evaluated in parallel
         // batches and appended in order.
-        if (env_flag("TCASPMM_HUB_WINDOWS", true)) {
+        if (env_flag("TCASPMM_HUB_WINDOWS", false)) {
             std::vector<int32_t> cand;
             for (int64_t r = 0; r < M; r++)
                 if (!S.row_tc[r] && A.row_ptr[r + 1] - A.row_ptr[r] >= 2 * S.tc.KT) cand.push_back((int32_t)r);

@@ -372,6 +372,7 @@ def test_gathered_windows_of_long_rows(dt, N, split, monkeypatch):
     """Long rows of a power-law graph grouped by length into tensor-core windows; their
     tile chains cut into parts of `split` tiles (reduced in part order), C written
     through the windows' row lists; N = 200 leaves a partial column block."""
+    monkeypatch.setenv("TCASPMM_HUB_WINDOWS", "1")
     monkeypatch.setenv("TCASPMM_SPLIT_TILES", split)
     A = T.gen_rmat(15, 400000, kind="gcn", seed=2)
     out, st = check(A, N, dt, seed=5)
@@ -381,6 +382,7 @@ def test_gathered_windows_of_long_rows(dt, N, split, monkeypatch):
 def test_gathered_windows_integer_values_bit_exact(monkeypatch):
     """Integer A and B small enough that every fp32 sum is exact: tiles, split parts
     and the fixed-order reduction must reproduce the oracle bit for bit."""
+    monkeypatch.setenv("TCASPMM_HUB_WINDOWS", "1")
     monkeypatch.setenv("TCASPMM_SPLIT_TILES", "5")
     A = T.gen_rmat(13, 120000, kind="gcn", seed=9)
     g = np.random.default_rng(9)
@@ -392,6 +394,7 @@ def test_gathered_windows_integer_values_bit_exact(monkeypatch):
 
 
 def test_gathered_windows_are_deterministic(monkeypatch):
+    monkeypatch.setenv("TCASPMM_HUB_WINDOWS", "1")
     monkeypatch.setenv("TCASPMM_SPLIT_TILES", "3")
     A = T.gen_rmat(14, 200000, kind="gcn", seed=6)
     B = T.gen_dense(A.ncol, 128, 2, "f32")
@@ -402,6 +405,7 @@ def test_gathered_windows_are_deterministic(monkeypatch):
 
 
 def test_gathered_windows_with_unaligned_b_fall_back(monkeypatch):
+    monkeypatch.setenv("TCASPMM_HUB_WINDOWS", "1")
     A = T.gen_rmat(14, 200000, kind="gcn", seed=6)
     B = T.gen_dense(A.ncol, 64, 2, "f32")
     out, st = run(A, B, "f16", ldb_pad=3)  # ldb = 67 halves: rows not 16-byte aligned
@@ -412,6 +416,7 @@ def test_gathered_windows_with_unaligned_b_fall_back(monkeypatch):
 def test_gathered_windows_switched_off_gives_the_same_product(monkeypatch):
     A = T.gen_rmat(14, 200000, kind="gcn", seed=7)
     B = T.gen_dense(A.ncol, 128, 4, "f32")
+    monkeypatch.setenv("TCASPMM_HUB_WINDOWS", "1")
     on, st_on = run(A, B, "f16")
     monkeypatch.setenv("TCASPMM_HUB_WINDOWS", "0")
     off, st_off = run(A, B, "f16")

@@ -314,21 +314,27 @@ def test_binary_csr_roundtrip(tmp_path):
 def test_gathered_windows_cover_long_rows_exactly_once(case, dt, N):
     """Long rows grouped by length into tensor-core windows (row lists): every nonzero
     is still covered exactly once, and the windows appear in the stats."""
+    os.environ["TCASPMM_HUB_WINDOWS"] = "1"
     if case == "gcn":
         A = T.gen_rmat(15, 400000, kind="gcn", seed=2)
     elif case == "sage":
         A = T.gen_rmat(15, 400000, kind="sage", seed=3)
     else:
         A = T.gen_skew(100000, 16, 20000, 3.0, seed=4)
-    cover, kind, st = T.schedule_coverage(A, N, dt)
+    try:
+        cover, kind, st = T.schedule_coverage(A, N, dt)
+    finally:
+        del os.environ["TCASPMM_HUB_WINDOWS"]
     assert np.all(cover == 1), np.bincount(cover)
     assert st["tc_gathered_windows"] > 0, st
     assert st["tc_nnz"] + st["residue_nnz"] == A.nnz
     assert (kind == 3).sum() == st["tc_nnz"]
 
 
-def test_gathered_windows_can_be_switched_off(monkeypatch):
+def test_gathered_windows_are_off_unless_asked_for(monkeypatch):
     A = T.gen_rmat(15, 400000, kind="gcn", seed=2)
-    monkeypatch.setenv("TCASPMM_HUB_WINDOWS", "0")
+    monkeypatch.delenv("TCASPMM_HUB_WINDOWS", raising=False)
     cover, _, st = T.schedule_coverage(A, 128, "f16")
     assert np.all(cover == 1) and st["tc_gathered_windows"] == 0
+    monkeypatch.setenv("TCASPMM_HUB_WINDOWS", "0")
+    assert T.schedule_coverage(A, 128, "f16")[2]["tc_gathered_windows"] == 0
