@@ -133,22 +133,6 @@ tcaspmm_status build_shard(const tcaspmm_csr &Afull, tcaspmm_dtype dt, int devic
             sh->val = d;
         }
     }
-    // Packed {column, value} pairs for the PK residue kernels: the value is the
-    // dtype-rounded value widened to fp32 (exact), so both index streams give
-    // the same products.
-    if (env_flag("TCASPMM_PACKED", false) && A.nnz > 0) {
-        std::vector<int2> pr((size_t)A.nnz);
-#pragma omp parallel for schedule(static)
-        for (int64_t j = 0; j < A.nnz; j++) {
-            float v = A.val ? A.val[j] : 1.0f;
-            if (dt == TCASPMM_F16) v = half_bits_to_float(float_to_half_bits(v));
-            if (dt == TCASPMM_BF16) v = bf16_bits_to_float(float_to_bf16_bits(v));
-            int vb;
-            std::memcpy(&vb, &v, 4);
-            pr[j] = make_int2(A.col_idx[j], vb);
-        }
-        if ((s = upload(*sh, &sh->pairs, pr.data(), pr.size(), "column/value pairs")) != TCASPMM_OK) return s;
-    }
     // Residue schedule and its scratch (partials + counters).
     const ResidueSchedule &RS = S.res;
     static_assert(sizeof(Int2) == sizeof(int2) && sizeof(Int4) == sizeof(int4), "layout");
@@ -215,7 +199,6 @@ tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB,
     p.segs = (const int4 *)sh.segs;
     p.n_segs = n_segs;
     p.longs = (const int4 *)sh.longs;
-    p.pairs = sh.pairs;
     p.partials = sh.partials;
     p.pstride = sh.pstride;
     p.counters = sh.counters;
@@ -224,7 +207,7 @@ tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB,
         p.ep = EpiParams{ep->row_scale, ep->bias, ep->relu, ep->out};
         launch_residue_epi(dt, vec, G, p, total, st);
     } else {
-        launch_res_dt<false>(dt, vec, G, p, total, st, sh.pairs != nullptr);
+        launch_res_dt<false>(dt, vec, G, p, total, st);
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "residue kernel launch");

@@ -31,9 +31,6 @@ struct Shard {
     int long_thr = 0;
     float *partials = nullptr;
     int pstride = 0;
-    // Packed {column, value bits} per nonzero for the PK residue kernels (one
-    // 8-byte index load per nonzero); null when the plan does not use them.
-    int2 *pairs = nullptr;
     unsigned int *counters = nullptr;
 
     // Tensor-core windows and the tasks they are cut into.

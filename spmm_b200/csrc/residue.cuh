@@ -49,7 +49,6 @@ struct ResidueParams {
     const int4 *__restrict__ segs;   // {row, begin, end, long id}
     int n_segs;
     const int4 *__restrict__ longs;  // {row, first seg, number of segs, 0}
-    const int2 *__restrict__ pairs;  // per nonzero {column, value as fp32 bits} (the PK kernels)
     float *partials;                 // n_segs x pstride
     int pstride;
     unsigned int *counters;          // one per long row, zero between launches
@@ -234,67 +233,44 @@ __device__ __forceinline__ void emit(const ResidueParams &p, long long r, int c0
         store_c<VEC>(p.C + r * p.ldc + c0, a);
 }
 
-// Index stream: the column of nonzero j, or with PK its packed {column, value
-// bits} pair (one 8-byte load in place of two).
-template <bool PK> using IdxT = typename std::conditional<PK, int2, int>::type;
-template <bool PK>
-__device__ __forceinline__ IdxT<PK> load_idx(const ResidueParams &p, int j)
-{
-    if constexpr (PK)
-        return __ldg(p.pairs + j);
-    else
-        return __ldg(p.col + j);
-}
-// Column and value of nonzero j from its index entry q (PK) or q plus a load of
-// the value array.
-template <typename T, bool PK>
-__device__ __forceinline__ void split_idx(const ResidueParams &p, int j, IdxT<PK> q, int &c, float &v)
-{
-    if constexpr (PK) {
-        c = q.x;
-        v = __int_as_float(q.y);
-    } else {
-        c = q;
-        v = to_f<T>(__ldg(static_cast<const T *>(p.val) + j));
-    }
-}
-
 // acc += sum_{j in [b, e)} val[j] * B[col[j]][c0 .. c0+VEC): full chunks of U
 // without predicates (U indices, U independent B loads, U FMAs), then the
 // remainder one nonzero at a time.
-template <typename T, int VEC, int U, bool PF = false, bool PK = false>
+template <typename T, int VEC, int U, bool PF = false>
 __device__ __forceinline__ void accumulate_lean(const ResidueParams &p, int b, const int e, int c0, float (&acc)[VEC])
 {
     const char *Bb = reinterpret_cast<const char *>(static_cast<const T *>(p.B) + c0);
     const unsigned pitch = (unsigned)(p.ldb * (long long)sizeof(T));
-    IdxT<PK> cn[U];  // PF: index entries of the next full chunk, loaded one chunk ahead
+    const T *__restrict__ val = static_cast<const T *>(p.val);
+    int cn[U];  // PF: columns of the next full chunk, loaded one chunk ahead
     if constexpr (PF) {
         if (b + U <= e)
 #pragma unroll
-            for (int u = 0; u < U; ++u) cn[u] = load_idx<PK>(p, b + u);
+            for (int u = 0; u < U; ++u) cn[u] = __ldg(p.col + b + u);
     }
     for (; b + U <= e; b += U) {
         int cc[U];
         float vv[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) split_idx<T, PK>(p, b + u, PF ? cn[u] : load_idx<PK>(p, b + u), cc[u], vv[u]);
+        for (int u = 0; u < U; ++u) {
+            cc[u] = PF ? cn[u] : __ldg(p.col + b + u);
+            vv[u] = to_f<T>(__ldg(val + b + u));
+        }
         Raw<T, VEC> rb[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) load_raw<T, VEC>(brow<T>(Bb, cc[u], pitch), rb[u]);
         if constexpr (PF) {
             if (b + 2 * U <= e)
 #pragma unroll
-                for (int u = 0; u < U; ++u) cn[u] = load_idx<PK>(p, b + U + u);
+                for (int u = 0; u < U; ++u) cn[u] = __ldg(p.col + b + U + u);
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) fma_raw<T, VEC>(vv[u], rb[u], acc);
     }
     for (; b < e; ++b) {
         Raw<T, VEC> rb;
-        int c;
-        float v;
-        split_idx<T, PK>(p, b, load_idx<PK>(p, b), c, v);
-        load_raw<T, VEC>(brow<T>(Bb, c, pitch), rb);
+        const float v = to_f<T>(__ldg(val + b));
+        load_raw<T, VEC>(brow<T>(Bb, __ldg(p.col + b), pitch), rb);
         fma_raw<T, VEC>(v, rb, acc);
     }
 }
@@ -303,12 +279,13 @@ __device__ __forceinline__ void accumulate_lean(const ResidueParams &p, int b, c
 // run without predicates (U indices, U B loads, U FMAs with a row-end check),
 // the remainder one nonzero at a time; each row is written when the stream
 // passes its end, trailing empty rows too.
-template <typename T, int VEC, int U, bool EPI, bool PF = false, bool PK = false>
+template <typename T, int VEC, int U, bool EPI, bool PF = false>
 __device__ __forceinline__ void stream_lean(const ResidueParams &p, int r_lo, int r_hi, int c0)
 {
     if (r_lo >= r_hi) return;
     const char *Bb = reinterpret_cast<const char *>(static_cast<const T *>(p.B) + c0);
     const unsigned pitch = (unsigned)(p.ldb * (long long)sizeof(T));
+    const T *__restrict__ val = static_cast<const T *>(p.val);
     int r = r_lo;
     int e = __ldg(p.row_ptr + r + 1);
     // PF: end of the next row, loaded one row ahead, so passing a row end does
@@ -338,24 +315,27 @@ __device__ __forceinline__ void stream_lean(const ResidueParams &p, int r_lo, in
             er.load_scale(p, r);
         }
     };
-    IdxT<PK> cn[U];  // PF: index entries of the next full chunk, loaded one chunk ahead
+    int cn[U];  // PF: columns of the next full chunk, loaded one chunk ahead
     if constexpr (PF) {
         if (j + U <= jend)
 #pragma unroll
-            for (int u = 0; u < U; ++u) cn[u] = load_idx<PK>(p, j + u);
+            for (int u = 0; u < U; ++u) cn[u] = __ldg(p.col + j + u);
     }
     for (; j + U <= jend; j += U) {
         int cc[U];
         float vv[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) split_idx<T, PK>(p, j + u, PF ? cn[u] : load_idx<PK>(p, j + u), cc[u], vv[u]);
+        for (int u = 0; u < U; ++u) {
+            cc[u] = PF ? cn[u] : __ldg(p.col + j + u);
+            vv[u] = to_f<T>(__ldg(val + j + u));
+        }
         Raw<T, VEC> rb[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) load_raw<T, VEC>(brow<T>(Bb, cc[u], pitch), rb[u]);
         if constexpr (PF) {
             if (j + 2 * U <= jend)
 #pragma unroll
-                for (int u = 0; u < U; ++u) cn[u] = load_idx<PK>(p, j + U + u);
+                for (int u = 0; u < U; ++u) cn[u] = __ldg(p.col + j + U + u);
         }
         if (j + U <= e) {  // the whole chunk lies in the current row: no row-end checks
 #pragma unroll
@@ -370,10 +350,8 @@ __device__ __forceinline__ void stream_lean(const ResidueParams &p, int r_lo, in
     }
     for (; j < jend; ++j) {
         Raw<T, VEC> rb;
-        int c;
-        float v;
-        split_idx<T, PK>(p, j, load_idx<PK>(p, j), c, v);
-        load_raw<T, VEC>(brow<T>(Bb, c, pitch), rb);
+        const float v = to_f<T>(__ldg(val + j));
+        load_raw<T, VEC>(brow<T>(Bb, __ldg(p.col + j), pitch), rb);
         pass_row_ends(j);
         fma_raw<T, VEC>(v, rb, acc);
     }
@@ -402,7 +380,7 @@ __device__ __forceinline__ int first_row_at(const int32_t *row_ptr, int lo, int 
 // measured faster than 40 registers / 48 warps and than 80 / 24 on GCN, SAGE
 // and the skew config, the epilogue instantiations included (at 80 registers
 // they ran 25% slower on GCN for the lost occupancy).
-template <typename T, int VEC, int G, int U, bool EPI, bool PF = false, int BLOCK = 256, bool PK = false>
+template <typename T, int VEC, int G, int U, bool EPI, bool PF = false, int BLOCK = 256>
 __global__ void __launch_bounds__(BLOCK, 1024 / BLOCK) residue_kernel(const ResidueParams p)
 {
     constexpr int P = 32 / G;
@@ -424,7 +402,7 @@ __global__ void __launch_bounds__(BLOCK, 1024 / BLOCK) residue_kernel(const Resi
             float acc[VEC];
 #pragma unroll
             for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
-            if (c0 < p.ncols) accumulate_lean<T, VEC, U, PF, PK>(p, jb, je, c0, acc);
+            if (c0 < p.ncols) accumulate_lean<T, VEC, U, PF>(p, jb, je, c0, acc);
 #pragma unroll
             for (int off = G; off < 32; off <<= 1)
 #pragma unroll
@@ -484,7 +462,7 @@ __global__ void __launch_bounds__(BLOCK, 1024 / BLOCK) residue_kernel(const Resi
     for (int pass = 0; pass < npass; ++pass) {
         const int c0 = pass * CPP + gl * VEC;
         if (c0 >= p.ncols) break;
-        stream_lean<T, VEC, U, EPI, PF, PK>(p, r_lo, r_hi, c0);
+        stream_lean<T, VEC, U, EPI, PF>(p, r_lo, r_hi, c0);
     }
 }
 

@@ -17,12 +17,12 @@ template <typename T, bool EPI> constexpr int unroll() { return EPI && sizeof(T)
 // flight per lane group, PF = columns and row ends loaded one chunk / one row
 // ahead.  With PF, 64 registers hold U = 7 for fp32 and U = 6 for 16-bit types
 // (6 for fp32 with the epilogue); beyond that the kernels spill.
-template <typename T, int VEC, int G, bool EPI, bool PF, int BLOCK, int U = unroll<T, EPI>(), bool PK = false>
+template <typename T, int VEC, int G, bool EPI, bool PF, int BLOCK, int U = unroll<T, EPI>()>
 void launch_res_v(const ResidueParams &p, int total_warps, cudaStream_t st)
 {
     constexpr int W = BLOCK / 32;
     const int blocks = (total_warps + W - 1) / W;
-    residue_kernel<T, VEC, G, U, EPI, PF, BLOCK, PK><<<blocks, BLOCK, 0, st>>>(p);
+    residue_kernel<T, VEC, G, U, EPI, PF, BLOCK><<<blocks, BLOCK, 0, st>>>(p);
 }
 
 // Shapes used (all measured on one B200, outputs bit-identical across shapes):
@@ -38,22 +38,9 @@ void launch_res_v(const ResidueParams &p, int total_warps, cudaStream_t st)
 //   epilogue kernels: prefetch, U = 6 for fp32, none for 16-bit, whose epilogue
 //   operands leave no registers for it (GCN f32 / f16 with the epilogue 1.90 /
 //   1.56 -> 1.68 / 1.42).
-//   with `pk` (packed {column, value} pairs, vector paths without the
-//   epilogue): one 8-byte index load per nonzero in place of two.
 template <typename T, int VEC, int G, bool EPI>
-void launch_res(const ResidueParams &p, int total_warps, cudaStream_t st, bool pk)
+void launch_res(const ResidueParams &p, int total_warps, cudaStream_t st)
 {
-    if constexpr (VEC > 1 && !EPI) {
-        if (pk) {
-            if constexpr (sizeof(T) == 4)
-                launch_res_v<T, VEC, G, EPI, true, 128, 6, true>(p, total_warps, st);
-            else if constexpr (G == 32)
-                launch_res_v<T, VEC, G, EPI, false, 128, 7, true>(p, total_warps, st);
-            else
-                launch_res_v<T, VEC, G, EPI, true, 128, 5, true>(p, total_warps, st);
-            return;
-        }
-    }
     if constexpr (VEC > 1 && !EPI) {
         if constexpr (sizeof(T) == 4)
             launch_res_v<T, VEC, G, EPI, true, 128, 7>(p, total_warps, st);
@@ -73,37 +60,36 @@ void launch_res(const ResidueParams &p, int total_warps, cudaStream_t st, bool p
 }
 
 template <typename T, int VEC, bool EPI>
-void launch_res_g(int G, const ResidueParams &p, int total_warps, cudaStream_t st, bool pk)
+void launch_res_g(int G, const ResidueParams &p, int total_warps, cudaStream_t st)
 {
     switch (G) {
-    case 1: launch_res<T, VEC, 1, EPI>(p, total_warps, st, pk); break;
-    case 2: launch_res<T, VEC, 2, EPI>(p, total_warps, st, pk); break;
-    case 4: launch_res<T, VEC, 4, EPI>(p, total_warps, st, pk); break;
-    case 8: launch_res<T, VEC, 8, EPI>(p, total_warps, st, pk); break;
-    case 16: launch_res<T, VEC, 16, EPI>(p, total_warps, st, pk); break;
-    default: launch_res<T, VEC, 32, EPI>(p, total_warps, st, pk); break;
+    case 1: launch_res<T, VEC, 1, EPI>(p, total_warps, st); break;
+    case 2: launch_res<T, VEC, 2, EPI>(p, total_warps, st); break;
+    case 4: launch_res<T, VEC, 4, EPI>(p, total_warps, st); break;
+    case 8: launch_res<T, VEC, 8, EPI>(p, total_warps, st); break;
+    case 16: launch_res<T, VEC, 16, EPI>(p, total_warps, st); break;
+    default: launch_res<T, VEC, 32, EPI>(p, total_warps, st); break;
     }
 }
 
 template <typename T, bool EPI>
-void launch_res_t(bool vec, int G, const ResidueParams &p, int total_warps, cudaStream_t st, bool pk)
+void launch_res_t(bool vec, int G, const ResidueParams &p, int total_warps, cudaStream_t st)
 {
     if (vec)
-        launch_res_g<T, 16 / sizeof(T), EPI>(G, p, total_warps, st, pk);
+        launch_res_g<T, 16 / sizeof(T), EPI>(G, p, total_warps, st);
     else
-        launch_res_g<T, 1, EPI>(G, p, total_warps, st, false);
+        launch_res_g<T, 1, EPI>(G, p, total_warps, st);
 }
 
 template <bool EPI>
-void launch_res_dt(tcaspmm_dtype dt, bool vec, int G, const ResidueParams &p, int total_warps, cudaStream_t st,
-                   bool pk = false)
+void launch_res_dt(tcaspmm_dtype dt, bool vec, int G, const ResidueParams &p, int total_warps, cudaStream_t st)
 {
     if (dt == TCASPMM_F32 || dt == TCASPMM_TF32)
-        launch_res_t<float, EPI>(vec, G, p, total_warps, st, pk);
+        launch_res_t<float, EPI>(vec, G, p, total_warps, st);
     else if (dt == TCASPMM_F16)
-        launch_res_t<__half, EPI>(vec, G, p, total_warps, st, pk);
+        launch_res_t<__half, EPI>(vec, G, p, total_warps, st);
     else
-        launch_res_t<__nv_bfloat16, EPI>(vec, G, p, total_warps, st, pk);
+        launch_res_t<__nv_bfloat16, EPI>(vec, G, p, total_warps, st);
 }
 
 }  // namespace tca

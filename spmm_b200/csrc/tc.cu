@@ -99,7 +99,9 @@ template <int FMT> struct Geo {
     static_assert(IDX_TILES % TPS == 0, "stages must not straddle index refills");
 };
 constexpr int TMEM_COLS = 2 * R;  // two accumulators
-constexpr int NPROD = 2;  // producer warps, taking stages round-robin
+constexpr int NPROD = 4;  // producer warps: TMA stages round-robin, cp.async stages together
+constexpr int PTHREADS = NPROD * 32;
+constexpr int CP_DEPTH = 3;  // cp.async stages in flight per producer thread (< STAGES)
 constexpr int NUM_THREADS = 160 + 32 * NPROD;
 constexpr int CBUF_BYTES = 4 * 32 * 32 * 4;  // C staging: a 32 x 32 fp32 tile per epilogue warp
 constexpr int EPI_THREADS = 128;
@@ -169,6 +171,28 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, vola
             return false;
         }
     }
+}
+
+__device__ __forceinline__ void mbar_arrive_n(uint32_t bar, uint32_t count)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+// 16-byte asynchronous copy global -> shared (L2 only); src_bytes 0 writes zeros.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Wait until at most n of this thread's cp.async groups are pending (n < CP_DEPTH).
+__device__ __forceinline__ void cp_async_wait(int n)
+{
+    if (n <= 0)
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+    else if (n == 1)
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else
+        asm volatile("cp.async.wait_group 2;" ::: "memory");
 }
 
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
@@ -361,7 +385,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     if (tid == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(smem_u32(&full[s]), 1);  // the producer's arrive.expect_tx; TMA completes the bytes
+            // One arrival per producer thread: a TMA stage's issuer arrives with
+            // expect_tx plus PTHREADS - 1 more (TMA completes the bytes); in a
+            // cp.async stage every producer thread arrives once its copies landed.
+            mbar_init(smem_u32(&full[s]), PTHREADS);
             mbar_init(smem_u32(&empty[s]), 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -385,24 +412,45 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     if (warp >= 5) {
         // ------------------------------ producers ------------------------------
-        // Warps 5 .. 5 + NPROD - 1 walk the same stage sequence; warp 5 + i
-        // fills the stages g with g % NPROD == i (one TMA issuer per warp).
-        // The warp stages the B-row indices of up to IDX_TILES tiles in shared
-        // memory with one coalesced load; lane 0 then fills one stage per TPS
-        // tiles: one 64 x 64 box per column half when the stage's 64 B rows are
-        // consecutive, else per tile a 64 x 16 box (16 consecutive rows) or four
-        // gather4 loads, plus one bulk copy of the stage's value tiles.  Abort
-        // decisions are warp-uniform.
+        // Warps 5 .. 5 + NPROD - 1 walk the same stage sequence.
+        //  * TMA stages (windows whose columns are one consecutive run, and the
+        //    tf32 gathers): warp 5 + i fills the stages g with g % NPROD == i from
+        //    one lane -- one 64 x 64 box per column piece when the stage's B rows
+        //    are consecutive, else per tile a 64 x 16 box or four gather4 loads,
+        //    plus one bulk copy of the stage's value tiles -- and arrives for all
+        //    producer threads.
+        //  * cp.async stages (gathered 16-bit tiles): all PTHREADS threads copy
+        //    the stage's B row slices (16 bytes each, coalesced per row) straight
+        //    into the 128-byte-swizzled panel layout, and the value tiles; each
+        //    thread keeps up to CP_DEPTH stages in flight and arrives on a stage's
+        //    full barrier once its own copies of that stage landed (after a proxy
+        //    fence, so the tensor cores see them).
         const int pw = warp - 5;
+        const int ptid = tid - 160;  // 0 .. PTHREADS - 1
         int32_t *myidx = idxbuf + pw * IDX_TILES * KT;
         uint32_t g = 0;  // stages of this CTA (issued by this warp or the other producers)
         bool ok = true;
+        uint32_t g_pend = 0;  // oldest of this thread's cp.async stages not yet arrived on
+        int npend = 0;
+        uint32_t tma_mine = 0;  // bit s: this lane issued the TMA copies of the stage now in slot s
+        auto release_oldest = [&](int keep) {
+            // This thread's copies of its oldest pending stage have landed once at
+            // most `keep` groups remain; make them visible to the async proxy and
+            // count this thread in.
+            cp_async_wait(keep);
+            fence_proxy_async();
+            mbar_arrive(smem_u32(&full[g_pend % STAGES]));
+            ++g_pend;
+            --npend;
+        };
         const void *tm_g = &maps.gather, *tm_16 = &maps.box16, *tm_64 = &maps.box64;
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(tm_g) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(tm_16) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(tm_64) : "memory");
         }
+        const char *Bbytes = static_cast<const char *>(p.B);
+        const long long pitch = p.ldb * G::ES;
         for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x) {
             const int win = u / p.nfb;  // task
             const bool first = u == (int)blockIdx.x;
@@ -411,11 +459,63 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int n0 = (u % p.nfb) * MB;
             const int nst = (w.z + G::TPS - 1) / G::TPS;  // stages of this unit (w.z >= 1)
             const int rot = win % nst;
+            if (c0 < 0 && FMT != 2) {
+                // Gathered 16-bit tiles through cp.async: thread ptid copies the
+                // 16-byte chunk cc = ptid % 16 of B rows k = ptid / 16 + 8 i.
+                const int cc = ptid & 15, pc = cc >> 3, c = cc & 7;
+                const int col = n0 + cc * 8;  // first of the chunk's 8 columns
+                const bool colok = col < p.ncols;
+                for (int k = 0; k < nst; ++k, ++g) {
+                    const int t = stage_at(k, rot, nst) * G::TPS;
+                    const int s = g % STAGES;
+                    const int n = min(G::TPS, w.z - t);
+                    // Abort decisions stay warp-uniform (the lanes of a producer warp
+                    // walk the same stages).
+                    ok = __all_sync(0xffffffffu, wait_bounded(smem_u32(&empty[s]), ((g / STAGES) & 1) ^ 1,
+                                                              abort_flag, p.err, 1, p.wait_cycles));
+                    if (!ok) break;
+                    tma_mine &= ~(1u << s);
+                    if (p.stall_test) continue;  // self-test: nothing copied, nothing arrives
+                    const uint32_t panel = smem_u32(smem + s * STAGE_BYTES);
+                    const int32_t *tcols = p.tile_cols + ((long long)w.y + t) * KT;
+                    const int rows = n * KT;
+                    int brow[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int kr = (ptid >> 4) + 8 * i;
+                        brow[i] = kr < rows ? __ldg(tcols + kr) : 0;
+                    }
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int kr = (ptid >> 4) + 8 * i;
+                        if (kr < rows) {
+                            const uint32_t dst = panel + pc * G::PIECE + (kr >> 3) * 1024 + (kr & 7) * 128 +
+                                                 ((c ^ (kr & 7)) << 4);
+                            const char *src = colok ? Bbytes + (long long)brow[i] * pitch + (long long)col * G::ES
+                                                    : Bbytes;
+                            cp_async16(dst, src, colok ? 16u : 0u);
+                        }
+                    }
+                    const uint8_t *vsrc = p.tile_vals + ((long long)w.y + t) * G::TILE_VAL;
+                    for (int q = ptid; q < n * (G::TILE_VAL / 16); q += PTHREADS)
+                        cp_async16(panel + PANEL_BYTES + q * 16, vsrc + q * 16, 16u);
+                    cp_async_commit();
+                    ++npend;
+                    if (npend == CP_DEPTH) release_oldest(CP_DEPTH - 1);
+                }
+                // Before a TMA task (or the end) every pending stage is released.
+                const int un = u + gridDim.x;
+                const bool next_cp = ok && un < p.n_units && p.dense_c0[un / p.nfb] < 0;
+                if (!next_cp)
+                    while (npend > 0) release_oldest(npend - 1);
+                continue;
+            }
             if (c0 >= 0) {
                 // One consecutive run of columns c0, c0 + 1, ...: tile t covers B
                 // rows c0 + 16 t .. + 15 (rows past the run have zero values, rows
                 // past K are zero-filled by TMA), so no indices are loaded.
                 for (int k = 0; ok && k < nst; ++k, ++g) {
+                    tma_mine &= ~(1u << (g % STAGES));
                     if ((int)(g % NPROD) != pw) continue;
                     const int t = stage_at(k, rot, nst) * G::TPS;
                     const int s = g % STAGES;
@@ -439,6 +539,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         }
                         bulk_copy(panel + PANEL_BYTES, p.tile_vals + ((long long)w.y + t) * G::TILE_VAL,
                                   (uint32_t)n * G::TILE_VAL, fb);
+                        mbar_arrive_n(fb, PTHREADS - 1);
+                        tma_mine |= 1u << s;
                     }
                 }
                 continue;
@@ -454,6 +556,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         myidx[q] = __ldg(p.tile_cols + ((long long)w.y + t0) * KT + q);
                     __syncwarp();  // indices visible to the warp
                 }
+                tma_mine &= ~(1u << (g % STAGES));
                 if ((int)(g % NPROD) != pw) continue;
                 const int s = g % STAGES;
                 const int n = min(G::TPS, w.z - t);  // tiles in this stage
@@ -493,17 +596,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     }
                     bulk_copy(panel + PANEL_BYTES, p.tile_vals + ((long long)w.y + t) * G::TILE_VAL,
                               (uint32_t)n * G::TILE_VAL, fb);
+                    mbar_arrive_n(fb, PTHREADS - 1);
+                    tma_mine |= 1u << s;
                 }
             }
         }
-        // Drain: the copies of the last STAGES stages must have landed before the
-        // CTA may exit (already true unless the kernel is aborting).
-        if (lane == 0 && !p.stall_test) {
+        // Drain: this thread's cp.async copies have landed, and the TMA copies
+        // this lane issued for the last STAGES stages, before the CTA may exit
+        // (already true unless the kernel is aborting).
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        if (!p.stall_test) {
             int no_abort = 0;
             for (uint32_t k = g > (uint32_t)STAGES ? g - STAGES : 0; k < g; ++k)
-                if ((int)(k % NPROD) == pw)
+                if ((tma_mine >> (k % STAGES)) & 1u)
                     wait_bounded(smem_u32(&full[k % STAGES]), (k / STAGES) & 1, (volatile int *)&no_abort, p.err, 16,
-                             p.wait_cycles);
+                                 p.wait_cycles);
         }
         __syncwarp();
     } else if (warp == 4) {
@@ -658,7 +765,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // Tail: 2 * STAGES + 5 mbarriers, the TMEM address and the abort flag.
 constexpr size_t kBarBytes = (2 * STAGES + 5) * 8 + 8;
 constexpr size_t kSmemBytes =
-    1024 + STAGES * STAGE_BYTES + CBUF_BYTES + NPROD * IDX_TILES * KT * 4 + (kBarBytes + 127) / 128 * 128;  // ~103 KB
+    1024 + STAGES * STAGE_BYTES + CBUF_BYTES + NPROD * IDX_TILES * KT * 4 + (kBarBytes + 127) / 128 * 128;  // ~107 KB
 
 template <typename X>
 tcaspmm_status upload_vec(Shard *sh, X **dst, const std::vector<X> &v, const char *what)

@@ -61,7 +61,7 @@ def test_noalloc_matches_plan_entry_on_two_calls(case, dt, N):
     elif case == "wide":
         # nnz * 2 * N above the 4M floats of scratch: the chunk grows past its 256-nonzero
         # minimum (about 500 here), so the scratch limit, not the floor, sets the split.
-        A = T.gen_skew(20000, 4, 50000, 3.0, seed=24)
+        A = T.gen_skew(50000, 4, 40000, 3.0, seed=24)
         assert -(-A.nnz // (4 * 2**20 // (2 * N))) > 256
     elif case == "gcn":
         A = T.gen_rmat(15, 200000, kind="gcn", seed=22)
