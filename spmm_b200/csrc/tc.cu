@@ -65,7 +65,8 @@ constexpr int R = 32;            // window rows = MMA N
 constexpr int KT = 16;           // condensed columns per tile
 constexpr int MB = 128;          // output columns per unit = MMA M
 constexpr int STAGES = 4;        // pipeline stages of 20 KB
-constexpr int IDX_TILES = 32;    // tile column indices staged per refill (a multiple of every TPS)
+constexpr int IDX_TILES = 16;    // tile column indices staged per refill (a multiple of every TPS); 16 keeps
+                                 // the shared memory of a CTA low enough for two CTAs per SM
 constexpr int PANEL_BYTES = 16384;                     // B panel per stage (any element type)
 constexpr int STAGE_BYTES = PANEL_BYTES + 4096;        // + the stage's value tiles
 
@@ -461,14 +462,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int rot = win % nst;
             if (c0 < 0 && FMT != 2) {
                 // Gathered 16-bit tiles through cp.async: thread ptid copies the
-                // 16-byte chunk cc = ptid % 16 of B rows k = ptid / 16 + 8 i.
+                // 16-byte chunk cc = ptid % 16 of B rows k = ptid / 16 + 8 i.  The
+                // B-row indices of the next stage are loaded one stage ahead, so
+                // issuing a stage never waits on an index load.
                 const int cc = ptid & 15, pc = cc >> 3, c = cc & 7;
                 const int col = n0 + cc * 8;  // first of the chunk's 8 columns
                 const bool colok = col < p.ncols;
+                int nxt[8];  // B rows of the next stage's rows k = ptid / 16 + 8 i
+                auto load_rows = [&](int k) {
+                    const int t = stage_at(k, rot, nst) * G::TPS;
+                    const int rows = min(G::TPS, w.z - t) * KT;
+                    const int32_t *tcols = p.tile_cols + ((long long)w.y + t) * KT;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int kr = (ptid >> 4) + 8 * i;
+                        nxt[i] = kr < rows ? __ldg(tcols + kr) : 0;
+                    }
+                };
+                load_rows(0);
                 for (int k = 0; k < nst; ++k, ++g) {
                     const int t = stage_at(k, rot, nst) * G::TPS;
                     const int s = g % STAGES;
                     const int n = min(G::TPS, w.z - t);
+                    int brow[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) brow[i] = nxt[i];
+                    if (k + 1 < nst) load_rows(k + 1);
                     // Abort decisions stay warp-uniform (the lanes of a producer warp
                     // walk the same stages).
                     ok = __all_sync(0xffffffffu, wait_bounded(smem_u32(&empty[s]), ((g / STAGES) & 1) ^ 1,
@@ -477,14 +496,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     tma_mine &= ~(1u << s);
                     if (p.stall_test) continue;  // self-test: nothing copied, nothing arrives
                     const uint32_t panel = smem_u32(smem + s * STAGE_BYTES);
-                    const int32_t *tcols = p.tile_cols + ((long long)w.y + t) * KT;
                     const int rows = n * KT;
-                    int brow[8];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const int kr = (ptid >> 4) + 8 * i;
-                        brow[i] = kr < rows ? __ldg(tcols + kr) : 0;
-                    }
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const int kr = (ptid >> 4) + 8 * i;
@@ -619,8 +631,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             constexpr uint32_t idesc = instr_desc<FMT>();
             uint32_t g = 0, i = 0;
             bool ok = true;
+            // Task descriptors are loaded one task ahead.
+            int4 wn = (int)blockIdx.x < p.n_units ? p.tasks[blockIdx.x / p.nfb] : make_int4(0, 0, 1, 0);
             for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x, ++i) {
-                const int4 w = p.tasks[u / p.nfb];
+                const int4 w = wn;
+                if (u + (int)gridDim.x < p.n_units) wn = p.tasks[(u + gridDim.x) / p.nfb];
                 const uint32_t a = i & 1;
                 if (!wait_bounded(smem_u32(&acce[a]), ((i >> 1) & 1) ^ 1, abort_flag, p.err, 2, p.wait_cycles)) break;
                 tc_fence_after();
@@ -669,7 +684,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t i = 0;
         for (int u = blockIdx.x; u < p.n_units; u += gridDim.x, ++i) {
             const int t = u / p.nfb, fb = u % p.nfb;
+            // The task's descriptor, split and row ids load while the MMAs run.
             const int4 w = p.tasks[t];
+            const int4 sp = p.splits[t];
+            // C row of the window's row `lane` (gathered windows read their row list).
+            const int rid = w.x >= 0 ? w.x + lane : (lane < w.w ? __ldg(p.rows + (-(w.x + 1)) + lane) : 0);
             const uint32_t a = i & 1;
             if (!__all_sync(0xffffffffu,
                             wait_bounded(smem_u32(&accf[a]), (i >> 1) & 1, abort_flag, p.err, 4, p.wait_cycles)))
@@ -679,7 +698,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + a * R, v);
             tc_fence_before();
             mbar_arrive(smem_u32(&acce[a]));
-            const int4 sp = p.splits[t];
             if (sp.x >= 0) {
                 // One part of a split window: publish this warp's 32 x 32 partial
                 // tile and count it in; the warp that completes the window's last
@@ -704,8 +722,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 if (lane == 0) *cnt = 0u;  // ready for the next launch
             }
-            // C row of the window's row `lane` (gathered windows read their row list).
-            const int rid = w.x >= 0 ? w.x + lane : (lane < w.w ? __ldg(p.rows + (-(w.x + 1)) + lane) : 0);
             if (p.has_ep && p.ep.row_scale) {
                 // One load of the window's row scales, then a broadcast per row
                 // (all lanes converged here).
@@ -765,7 +781,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // Tail: 2 * STAGES + 5 mbarriers, the TMEM address and the abort flag.
 constexpr size_t kBarBytes = (2 * STAGES + 5) * 8 + 8;
 constexpr size_t kSmemBytes =
-    1024 + STAGES * STAGE_BYTES + CBUF_BYTES + NPROD * IDX_TILES * KT * 4 + (kBarBytes + 127) / 128 * 128;  // ~107 KB
+    1024 + STAGES * STAGE_BYTES + CBUF_BYTES + NPROD * IDX_TILES * KT * 4 + (kBarBytes + 127) / 128 * 128;  // ~101 KB: two CTAs per SM
 
 template <typename X>
 tcaspmm_status upload_vec(Shard *sh, X **dst, const std::vector<X> &v, const char *what)
