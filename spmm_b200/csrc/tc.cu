@@ -929,18 +929,40 @@ tcaspmm_status tc_upload(const tcaspmm_csr &A, tcaspmm_dtype dt, Shard *sh)
         Int4 d, sp;
         int32_t dense;
     };
+    int nsm = 148;
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, sh->device);
+    sh->num_sms = nsm;
     std::vector<Task> tasks;
     int32_t groups = 0, slots = 0;
     const int split = (int)env_int("TCASPMM_SPLIT_TILES", SPLIT_TILES, 1, 4096);
+    // Consecutive windows stay whole unless they are too few to fill the GPU:
+    // with at most half as many work items as resident CTAs (two per SM), each
+    // is cut into parts (at least one stage of tiles each) so every CTA slot has
+    // one -- a shorter tile chain per CTA.  TCASPMM_WINDOW_PARTS (clamped to
+    // [0, 64]; 0 = this rule) sets the parts of a consecutive window instead.
+    const int64_t nfb_units = (sh->ncols + MB - 1) / MB;
+    int64_t n_consec = 0;
+    for (const Int4 &w : T.windows) n_consec += w.x >= 0;
+    const int64_t slots_gpu = 2 * (int64_t)sh->num_sms;
+    const int forced = (int)env_int("TCASPMM_WINDOW_PARTS", 0, 0, 64);
+    int consec_parts = 1;
+    if (forced > 0)
+        consec_parts = forced;
+    else if (n_consec > 0 && (int64_t)T.windows.size() * nfb_units * 2 <= slots_gpu)
+        consec_parts = (int)std::min<int64_t>(8, slots_gpu / ((int64_t)T.windows.size() * nfb_units));
     for (const Int4 &w : T.windows) {
-        const int parts = w.x >= 0 ? 1 : (w.z + split - 1) / split;
+        const int parts = w.x >= 0 ? std::max(1, std::min(consec_parts, (w.z + Geo<0>::TPS - 1) / Geo<0>::TPS))
+                                   : (w.z + split - 1) / split;
+        const int32_t dense = w.x >= 0 ? dense_run(w) : -1;
         if (parts == 1) {
-            tasks.push_back(Task{w, Int4{-1, 0, 1, 0}, w.x >= 0 ? dense_run(w) : -1});
+            tasks.push_back(Task{w, Int4{-1, 0, 1, 0}, dense});
             continue;
         }
         for (int q = 0; q < parts; q++) {
             const int32_t t0 = (int32_t)((int64_t)w.z * q / parts), t1 = (int32_t)((int64_t)w.z * (q + 1) / parts);
-            tasks.push_back(Task{Int4{w.x, w.y + t0, t1 - t0, w.w}, Int4{groups, q, parts, slots}, -1});
+            // A part of a consecutive run starts t0 tiles (16 t0 columns) into it.
+            tasks.push_back(Task{Int4{w.x, w.y + t0, t1 - t0, w.w}, Int4{groups, q, parts, slots},
+                                 dense >= 0 ? dense + t0 * KT : -1});
         }
         groups++;
         slots += parts;
@@ -1024,9 +1046,6 @@ tcaspmm_status tc_upload(const tcaspmm_csr &A, tcaspmm_dtype dt, Shard *sh)
         sh->allocs.push_back(sh->tc_partials);
         sh->bytes += (int64_t)pbytes;
     }
-    int nsm = 148;
-    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, sh->device);
-    sh->num_sms = nsm;
     // More than 48 KB of dynamic shared memory needs the opt-in, per device.
     cudaError_t e = smem_optin<0>();
     if (e == cudaSuccess) e = smem_optin<1>();

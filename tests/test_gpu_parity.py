@@ -423,3 +423,25 @@ def test_gathered_windows_switched_off_gives_the_same_product(monkeypatch):
     assert st_on["tc_gathered_windows"] > 0 and st_off["tc_gathered_windows"] == 0
     ref = reference(A, B, "f16")
     assert oracle.rel_l2(on, ref) <= TOL_TC and oracle.rel_l2(off, ref) <= TOL_TC
+
+
+@pytest.mark.parametrize("parts", ["0", "1", "3", "8"])
+@pytest.mark.parametrize("dt", ["f16", "tf32"])
+def test_consecutive_windows_cut_into_parts(parts, dt, monkeypatch):
+    """C1-shaped windows (consecutive rows, one consecutive column run) cut into 1, 3 or 8
+    parts of their tile chain (0: automatic, two parts here), reduced in part order."""
+    monkeypatch.setenv("TCASPMM_WINDOW_PARTS", parts)
+    out, st = check(T.gen_uniform(2048, 512, 0.3, 0), 256, dt)
+    assert st["tc_windows"] == 64
+    assert st["tc_tasks"] == (64 if parts == "1" else 64 * (2 if parts == "0" else int(parts))), st
+
+
+def test_consecutive_window_parts_integer_bit_exact(monkeypatch):
+    monkeypatch.setenv("TCASPMM_WINDOW_PARTS", "5")
+    g = np.random.default_rng(4)
+    A = T.gen_uniform(512, 512, 0.3, 4)
+    A = T.CSR(A.nrow, A.ncol, A.row_ptr, A.col, g.integers(-3, 4, A.nnz).astype(np.float32))
+    B = g.integers(-4, 5, (A.ncol, 128)).astype(np.float32)
+    out, st = run(A, B, "f16")
+    assert st["tc_tasks"] > st["tc_windows"] > 0
+    np.testing.assert_array_equal(out, reference(A, B, "f16"))
