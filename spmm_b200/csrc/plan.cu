@@ -150,8 +150,8 @@ tcaspmm_status build_shard(const tcaspmm_csr &Afull, tcaspmm_dtype dt, int devic
         e = cudaMemset(sh->counters, 0, sizeof(unsigned int) * sh->n_longs);
         if (e != cudaSuccess) return cuda_fail(e, "zero counters");
     }
-    if ((s = upload<int>(*sh, &sh->err, nullptr, 1, "error word")) != TCASPMM_OK) return s;
-    e = cudaMemset(sh->err, 0, sizeof(int));
+    if ((s = upload<int>(*sh, &sh->err, nullptr, 6, "error words")) != TCASPMM_OK) return s;
+    e = cudaMemset(sh->err, 0, 6 * sizeof(int));
     if (e != cudaSuccess) return cuda_fail(e, "zero error word");
     if ((s = tc_upload(A, dt, sh)) != TCASPMM_OK) return s;
     e = cudaDeviceSynchronize();
@@ -534,17 +534,20 @@ tcaspmm_status tcaspmm_plan_sync_check(tcaspmm_plan *plan)
         DeviceGuard g(sh.device);
         cudaError_t e = cudaDeviceSynchronize();
         if (e != cudaSuccess) return cuda_fail(e, "synchronize");
-        int err = 0;
-        e = cudaMemcpy(&err, sh.err, sizeof(int), cudaMemcpyDeviceToHost);
+        int err[6] = {0, 0, 0, 0, 0, 0};
+        e = cudaMemcpy(err, sh.err, sizeof(err), cudaMemcpyDeviceToHost);
         if (e != cudaSuccess) return cuda_fail(e, "read error word");
-        if (err != 0) {
-            cudaMemset(sh.err, 0, sizeof(int));
+        if (err[0] != 0) {
+            cudaMemset(sh.err, 0, sizeof(err));
             // An aborted launch may have left split windows part-counted: start
             // the next launch from zero.
             if (sh.tc_counters)
                 cudaMemset(sh.tc_counters, 0,
                            sizeof(unsigned int) * (size_t)sh.n_split_groups * ((sh.ncols + 127) / 128) * 4);
-            return fail(TCASPMM_ERR_TIMEOUT, "device %d: tensor-core kernel gave up waiting (code 0x%x)", sh.device, err);
+            return fail(TCASPMM_ERR_TIMEOUT,
+                        "device %d: tensor-core kernel gave up waiting (codes 0x%x; first: code %d on the barrier at "
+                        "shared address 0x%x, parity %d, CTA %d, thread %d)",
+                        sh.device, err[0], err[1], err[2], err[3], err[4], err[5]);
         }
     }
     return TCASPMM_OK;

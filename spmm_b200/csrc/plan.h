@@ -62,7 +62,7 @@ struct Shard {
     mutable int64_t cmap_ldc = 0;
     mutable int cmap_out = 0;
 
-    int *err = nullptr;  // device error word (bounded waits that ran out)
+    int *err = nullptr;  // device error words: codes of bounded waits that ran out, and where the first did
 };
 
 // Fused output epilogue of one launch (tcaspmm_epilogue after validation):

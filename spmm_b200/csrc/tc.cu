@@ -122,6 +122,7 @@ struct TcParams {
     void *C;                 // fp32, or 16-bit with the epilogue
     long long ldc;           // elements of C's type
     int ncols;
+    int K;                   // rows of B
     int n_units;
     int nfb;                 // column blocks of 128
     int *err;
@@ -158,6 +159,9 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar)
 }
 
 // Bounded wait: false (and the abort flag raised, error recorded) on time-out.
+// err[0] collects the codes of every wait that ran out; the first one also
+// records where it gave up: err[1] its code, err[2] the barrier's shared-memory
+// address, err[3] the phase parity waited for, err[4] the CTA, err[5] the thread.
 __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int *abort_flag, int *err,
                                              int code, unsigned long long limit)
 {
@@ -168,6 +172,12 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, vola
         if (*abort_flag) return false;
         if (clock64() - t0 > limit) {
             atomicOr(err, code);
+            if (atomicCAS(err + 1, 0, code) == 0) {
+                err[2] = (int)bar;
+                err[3] = (int)parity;
+                err[4] = (int)blockIdx.x;
+                err[5] = (int)threadIdx.x;
+            }
             *abort_flag = 1;
             return false;
         }
@@ -540,7 +550,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         const uint32_t panel = smem_u32(smem + s * STAGE_BYTES);
                         const int y = c0 + t * KT;
                         mbar_expect_tx(fb, (uint32_t)n * (G::TILE_PANEL + G::TILE_VAL));
-                        if (n == G::TPS) {
+                        // One box of a whole stage only when all its rows lie inside B;
+                        // a stage that runs past the last row takes a box per tile.
+                        if (n == G::TPS && y + G::SROWS <= p.K) {
 #pragma unroll
                             for (int c = 0; c < G::NPC; ++c) tma_box(panel + c * G::PIECE, tm_64, n0 + c * G::CPB, y, fb);
                         } else {
@@ -935,21 +947,11 @@ tcaspmm_status tc_upload(const tcaspmm_csr &A, tcaspmm_dtype dt, Shard *sh)
     std::vector<Task> tasks;
     int32_t groups = 0, slots = 0;
     const int split = (int)env_int("TCASPMM_SPLIT_TILES", SPLIT_TILES, 1, 4096);
-    // Consecutive windows stay whole unless they are too few to fill the GPU:
-    // with at most half as many work items as resident CTAs (two per SM), each
-    // is cut into parts (at least one stage of tiles each) so every CTA slot has
-    // one -- a shorter tile chain per CTA.  TCASPMM_WINDOW_PARTS (clamped to
-    // [0, 64]; 0 = this rule) sets the parts of a consecutive window instead.
-    const int64_t nfb_units = (sh->ncols + MB - 1) / MB;
-    int64_t n_consec = 0;
-    for (const Int4 &w : T.windows) n_consec += w.x >= 0;
-    const int64_t slots_gpu = 2 * (int64_t)sh->num_sms;
-    const int forced = (int)env_int("TCASPMM_WINDOW_PARTS", 0, 0, 64);
-    int consec_parts = 1;
-    if (forced > 0)
-        consec_parts = forced;
-    else if (n_consec > 0 && (int64_t)T.windows.size() * nfb_units * 2 <= slots_gpu)
-        consec_parts = (int)std::min<int64_t>(8, slots_gpu / ((int64_t)T.windows.size() * nfb_units));
+    // Consecutive windows stay whole by default (cutting C1's windows in two to
+    // fill all 296 CTA slots measured slower, 16.3 against 12.3 us per step);
+    // TCASPMM_WINDOW_PARTS (clamped to [1, 64]) cuts each into that many parts
+    // of its tile chain (at most one per stage of tiles).
+    const int consec_parts = (int)env_int("TCASPMM_WINDOW_PARTS", 1, 1, 64);
     for (const Int4 &w : T.windows) {
         const int parts = w.x >= 0 ? std::max(1, std::min(consec_parts, (w.z + Geo<0>::TPS - 1) / Geo<0>::TPS))
                                    : (w.z + split - 1) / split;
@@ -1078,6 +1080,7 @@ tcaspmm_status launch_tc(const Shard &sh, tcaspmm_dtype dt, const void *dB, int6
     p.C = dC;
     p.ldc = ldc;
     p.ncols = (int)sh.ncols;
+    p.K = (int)sh.K;
     p.nfb = (int)((sh.ncols + MB - 1) / MB);
     p.n_units = sh.n_tasks * p.nfb;
     p.err = sh.err;
@@ -1148,7 +1151,7 @@ extern "C" tcaspmm_status tcaspmm_selftest_tc_timeout(int device, unsigned long 
     alloc(&d_vals, vals.size() * 2);
     alloc(&d_b, Geo<0>::SROWS * MB * 2);
     alloc(&d_c, R * MB * 4);
-    alloc((void **)&d_err, sizeof(int));
+    alloc((void **)&d_err, 6 * sizeof(int));
     BMaps maps;
     if (st == TCASPMM_OK) {
         cudaMemcpy(d_win, &win, sizeof(win), cudaMemcpyHostToDevice);
@@ -1157,7 +1160,7 @@ extern "C" tcaspmm_status tcaspmm_selftest_tc_timeout(int device, unsigned long 
         cudaMemcpy(d_cols, cols.data(), cols.size() * 4, cudaMemcpyHostToDevice);
         cudaMemcpy(d_vals, vals.data(), vals.size() * 2, cudaMemcpyHostToDevice);
         cudaMemset(d_b, 0, Geo<0>::SROWS * MB * 2);
-        cudaMemset(d_err, 0, sizeof(int));
+        cudaMemset(d_err, 0, 6 * sizeof(int));
         st = encode_b_maps(TCASPMM_F16, d_b, MB, Geo<0>::SROWS, MB, &maps);
     }
     if (st == TCASPMM_OK) {

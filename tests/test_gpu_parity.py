@@ -425,15 +425,24 @@ def test_gathered_windows_switched_off_gives_the_same_product(monkeypatch):
     assert oracle.rel_l2(on, ref) <= TOL_TC and oracle.rel_l2(off, ref) <= TOL_TC
 
 
-@pytest.mark.parametrize("parts", ["0", "1", "3", "8"])
+@pytest.mark.parametrize("parts", ["1", "2", "3", "8"])
 @pytest.mark.parametrize("dt", ["f16", "tf32"])
 def test_consecutive_windows_cut_into_parts(parts, dt, monkeypatch):
-    """C1-shaped windows (consecutive rows, one consecutive column run) cut into 1, 3 or 8
-    parts of their tile chain (0: automatic, two parts here), reduced in part order."""
+    """C1-shaped windows (consecutive rows, one consecutive column run) cut into 1, 2, 3
+    or 8 parts of their tile chain, reduced in part order."""
     monkeypatch.setenv("TCASPMM_WINDOW_PARTS", parts)
     out, st = check(T.gen_uniform(2048, 512, 0.3, 0), 256, dt)
     assert st["tc_windows"] == 64
-    assert st["tc_tasks"] == (64 if parts == "1" else 64 * (2 if parts == "0" else int(parts))), st
+    assert st["tc_tasks"] == 64 * int(parts), st
+
+
+@pytest.mark.parametrize("parts", ["3", "5"])
+def test_window_parts_whose_last_stage_runs_past_b(parts, monkeypatch):
+    """K = 300: a part's four-tile stage can start within 64 rows of B's end; it must be
+    fetched tile by tile, not as one box past the last row."""
+    monkeypatch.setenv("TCASPMM_WINDOW_PARTS", parts)
+    _, st = check(T.gen_uniform(1000, 300, 0.4, 11), 72, "f16")
+    assert st["tc_tasks"] > st["tc_windows"] > 0
 
 
 def test_consecutive_window_parts_integer_bit_exact(monkeypatch):
