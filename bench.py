@@ -329,6 +329,8 @@ def main():
     ap.add_argument("--split", default="columns", choices=["columns", "rows", "2d"],
                     help="multi-GPU partition: column blocks of B/C (A replicated), row blocks of A/C "
                          "(B replicated), or a 2-D grid of both (--grid)")
+    ap.add_argument("--launch", default="graph", choices=["graph", "eager"],
+                    help="timed step: replay a CUDA graph of the plan's launches, or call execute directly")
     ap.add_argument("--grid", default=None,
                     help="RxC shard grid for --split 2d (default: two column blocks when N GPUs is even)")
     args = ap.parse_args()
@@ -418,17 +420,20 @@ def main():
     for _ in range(args.warmup):
         step()
     plan.sync_check()
-    # The timed step replays a CUDA graph of the plan's launches (same kernels,
-    # same arguments; launch latency paid once at capture).
-    graph = torch.cuda.CUDAGraph()
-    cap = torch.cuda.Stream(dev)
-    cap.wait_stream(stream)
-    with torch.cuda.graph(graph, stream=cap):
-        plan.execute1(Bd, Cd, cap, epilogue=ep)
-    stream.wait_stream(cap)
+    # With --launch graph (the default) the timed step replays a CUDA graph of the
+    # plan's launches (same kernels, same arguments; launch latency paid once at
+    # capture); with --launch eager it calls the C-ABI execute directly.
+    graph = None
+    if args.launch == "graph":
+        graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(stream)
+        with torch.cuda.graph(graph, stream=cap):
+            plan.execute1(Bd, Cd, cap, epilogue=ep)
+        stream.wait_stream(cap)
 
-    def step():  # noqa: F811 -- the graph replaces the eager launch from here on
-        graph.replay()
+        def step():  # noqa: F811 -- the graph replaces the eager launch from here on
+            graph.replay()
 
     for _ in range(2):
         step()
@@ -634,7 +639,8 @@ def main():
                        f"collective)",
                        "l2": "flushed between steps (2x L2 buffer)" if flush is not None
                        else "inputs larger than L2 (126 MB)",
-                       "launch": "CUDA graph of the plan's launches",
+                       "launch": "CUDA graph of the plan's launches" if graph is not None
+                       else "direct C-ABI execute per step",
                        "preprocess_ms": round(pst["preprocess_ms"], 3), "upload_ms": round(pst["upload_ms"], 3),
                        "tc_windows": pst["tc_windows"], "residue_segments": pst["residue_segments"],
                        **({"epilogue": "C = relu(row_scale * (A B) + bias) stored as bf16"} if args.epilogue

@@ -425,32 +425,16 @@ def test_gathered_windows_switched_off_gives_the_same_product(monkeypatch):
     assert oracle.rel_l2(on, ref) <= TOL_TC and oracle.rel_l2(off, ref) <= TOL_TC
 
 
-@pytest.mark.parametrize("parts", ["1", "2", "3", "8"])
-@pytest.mark.parametrize("dt", ["f16", "tf32"])
-def test_consecutive_windows_cut_into_parts(parts, dt, monkeypatch):
-    """C1-shaped windows (consecutive rows, one consecutive column run) cut into 1, 2, 3
-    or 8 parts of their tile chain, reduced in part order."""
-    monkeypatch.setenv("TCASPMM_WINDOW_PARTS", parts)
-    out, st = check(T.gen_uniform(2048, 512, 0.3, 0), 256, dt)
-    assert st["tc_windows"] == 64
-    assert st["tc_tasks"] == 64 * int(parts), st
-
-
-@pytest.mark.parametrize("parts", ["3", "5"])
-def test_window_parts_whose_last_stage_runs_past_b(parts, monkeypatch):
-    """K = 300: a part's four-tile stage can start within 64 rows of B's end; it must be
-    fetched tile by tile, not as one box past the last row."""
-    monkeypatch.setenv("TCASPMM_WINDOW_PARTS", parts)
-    _, st = check(T.gen_uniform(1000, 300, 0.4, 11), 72, "f16")
-    assert st["tc_tasks"] > st["tc_windows"] > 0
-
-
-def test_consecutive_window_parts_integer_bit_exact(monkeypatch):
-    monkeypatch.setenv("TCASPMM_WINDOW_PARTS", "5")
-    g = np.random.default_rng(4)
-    A = T.gen_uniform(512, 512, 0.3, 4)
-    A = T.CSR(A.nrow, A.ncol, A.row_ptr, A.col, g.integers(-3, 4, A.nnz).astype(np.float32))
-    B = g.integers(-4, 5, (A.ncol, 128)).astype(np.float32)
-    out, st = run(A, B, "f16")
-    assert st["tc_tasks"] > st["tc_windows"] > 0
-    np.testing.assert_array_equal(out, reference(A, B, "f16"))
+@pytest.mark.parametrize("K", [310, 316, 63 * 5])
+def test_dense_window_whose_last_stage_runs_past_b(K):
+    """Windows whose columns are one consecutive run: with K = 310 the run has 20 tiles,
+    so its last four-tile stage starts 54 rows before B ends; it is fetched tile by
+    tile rather than as one 64-row box past the last row."""
+    A = T.gen_uniform(256, K, 0.5, 12)
+    _, st = check(A, 128, "f16")
+    assert st["tc_windows"] > 0
+    g = np.random.default_rng(K)
+    Ai = T.CSR(A.nrow, A.ncol, A.row_ptr, A.col, g.integers(-3, 4, A.nnz).astype(np.float32))
+    B = g.integers(-4, 5, (K, 128)).astype(np.float32)
+    out, _ = run(Ai, B, "f16")
+    np.testing.assert_array_equal(out, reference(Ai, B, "f16"))
