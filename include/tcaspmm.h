@@ -100,6 +100,7 @@ typedef struct tcaspmm_plan_stats {
     int64_t algorithmic_bytes;/* A + B + C bytes (A: (M+1)*4 + nnz*(4+sizeof(val))) */
     int64_t tc_gathered_windows; /* tc windows of long rows grouped by length (row lists) */
     int64_t tc_tasks;         /* tensor-core work items per column block (windows split by tiles) */
+    int64_t tc_ctas_per_sm;   /* resident tensor-core CTAs per SM (the persistent grid is this x SMs) */
 } tcaspmm_plan_stats;
 
 /* ---------------------------------------------------------------- errors */

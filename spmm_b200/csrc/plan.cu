@@ -276,6 +276,7 @@ static tcaspmm_status create_common(const tcaspmm_csr *A, int64_t N, tcaspmm_dty
         st.tc_windows += (int64_t)Si.tc.windows.size();
         st.tc_gathered_windows += Si.tc.gathered;
         st.tc_tasks += P->shards[i]->n_tasks;
+        if (P->shards[i]->n_tasks) st.tc_ctas_per_sm = P->shards[i]->tc_ctas_per_sm;
         st.tc_tiles += Si.tc.KT ? (int64_t)Si.tc.tile_cols.size() / Si.tc.KT : 0;
         st.tc_nnz += Si.tc.nnz;
         st.residue_nnz += Si.res.nnz;
