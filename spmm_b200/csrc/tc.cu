@@ -363,8 +363,12 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// At most 96 registers a thread: the register file is split between the SM's
+// four schedulers (16K each), so two CTAs of nine warps (18 warps, five on one
+// scheduler) fit only at 96 or fewer (5 x 32 x 96 = 15360); at the 101 this kernel
+// takes unconstrained, one CTA per SM is resident.
 template <int FMT>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __maxnreg__(96)
     tc_kernel(const TcParams p, const __grid_constant__ BMaps maps, const __grid_constant__ CUtensorMap cmap)
 {
     extern __shared__ uint8_t smem_raw[];
