@@ -100,8 +100,15 @@ template <int FMT> struct Geo {
     static_assert(IDX_TILES % TPS == 0, "stages must not straddle index refills");
 };
 constexpr int TMEM_COLS = 2 * R;  // two accumulators
-constexpr int NPROD = 4;  // producer warps: TMA stages round-robin, cp.async stages together
+// Producer warps: TMA stages round-robin, cp.async stages together.  Three, so a
+// CTA has eight warps: warps are spread over the SM's four schedulers, whose
+// register files hold 16K registers each, and with eight warps two CTAs fit at up
+// to 128 registers a thread (nine warps put six on one scheduler: 85 at most).
+constexpr int NPROD = 3;
 constexpr int PTHREADS = NPROD * 32;
+constexpr int ROW_STEP = PTHREADS / 16;                     // B rows a cp.async pass covers (16 threads a row)
+constexpr int ROW_PASSES = (64 + ROW_STEP - 1) / ROW_STEP;  // passes over a stage's 64 rows
+static_assert(PTHREADS % 16 == 0, "a B row slice is copied by 16 threads");
 constexpr int CP_DEPTH = 3;  // cp.async stages in flight per producer thread (< STAGES)
 constexpr int NUM_THREADS = 160 + 32 * NPROD;
 constexpr int CBUF_BYTES = 4 * 32 * 32 * 4;  // C staging: a 32 x 32 fp32 tile per epilogue warp
@@ -363,12 +370,8 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// At most 96 registers a thread: the register file is split between the SM's
-// four schedulers (16K each), so two CTAs of nine warps (18 warps, five on one
-// scheduler) fit only at 96 or fewer (5 x 32 x 96 = 15360); at the 101 this kernel
-// takes unconstrained, one CTA per SM is resident.
 template <int FMT>
-__global__ void __maxnreg__(96)
+__global__ void __launch_bounds__(NUM_THREADS, 2)
     tc_kernel(const TcParams p, const __grid_constant__ BMaps maps, const __grid_constant__ CUtensorMap cmap)
 {
     extern __shared__ uint8_t smem_raw[];
@@ -476,20 +479,20 @@ __global__ void __maxnreg__(96)
             const int rot = win % nst;
             if (c0 < 0 && FMT != 2) {
                 // Gathered 16-bit tiles through cp.async: thread ptid copies the
-                // 16-byte chunk cc = ptid % 16 of B rows k = ptid / 16 + 8 i.  The
+                // 16-byte chunk cc = ptid % 16 of B rows k = ptid / 16 + ROW_STEP i.  The
                 // B-row indices of the next stage are loaded one stage ahead, so
                 // issuing a stage never waits on an index load.
                 const int cc = ptid & 15, pc = cc >> 3, c = cc & 7;
                 const int col = n0 + cc * 8;  // first of the chunk's 8 columns
                 const bool colok = col < p.ncols;
-                int nxt[8];  // B rows of the next stage's rows k = ptid / 16 + 8 i
+                int nxt[ROW_PASSES];  // B rows of the next stage's rows k = ptid / 16 + ROW_STEP i
                 auto load_rows = [&](int k) {
                     const int t = stage_at(k, rot, nst) * G::TPS;
                     const int rows = min(G::TPS, w.z - t) * KT;
                     const int32_t *tcols = p.tile_cols + ((long long)w.y + t) * KT;
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const int kr = (ptid >> 4) + 8 * i;
+                    for (int i = 0; i < ROW_PASSES; ++i) {
+                        const int kr = (ptid >> 4) + ROW_STEP * i;
                         nxt[i] = kr < rows ? __ldg(tcols + kr) : 0;
                     }
                 };
@@ -498,9 +501,9 @@ __global__ void __maxnreg__(96)
                     const int t = stage_at(k, rot, nst) * G::TPS;
                     const int s = g % STAGES;
                     const int n = min(G::TPS, w.z - t);
-                    int brow[8];
+                    int brow[ROW_PASSES];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) brow[i] = nxt[i];
+                    for (int i = 0; i < ROW_PASSES; ++i) brow[i] = nxt[i];
                     if (k + 1 < nst) load_rows(k + 1);
                     // Abort decisions stay warp-uniform (the lanes of a producer warp
                     // walk the same stages).
@@ -512,8 +515,8 @@ __global__ void __maxnreg__(96)
                     const uint32_t panel = smem_u32(smem + s * STAGE_BYTES);
                     const int rows = n * KT;
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const int kr = (ptid >> 4) + 8 * i;
+                    for (int i = 0; i < ROW_PASSES; ++i) {
+                        const int kr = (ptid >> 4) + ROW_STEP * i;
                         if (kr < rows) {
                             const uint32_t dst = panel + pc * G::PIECE + (kr >> 3) * 1024 + (kr & 7) * 128 +
                                                  ((c ^ (kr & 7)) << 4);
@@ -872,7 +875,13 @@ static_assert(sizeof(BMaps) <= sizeof(Shard::maps) && sizeof(CUtensorMap) <= siz
 template <int FMT>
 cudaError_t smem_optin()
 {
-    return cudaFuncSetAttribute(tc_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(tc_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    // The largest shared-memory carveout, so two CTAs of ~104 KB can be resident
+    // on an SM (left to itself the driver configures 135 KB: one CTA).
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(tc_kernel<FMT>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared);
+    return e;
 }
 
 void launch_kernel(int fmt, int grid, const TcParams &p, const BMaps &maps, const CUtensorMap &cmap, cudaStream_t st)
