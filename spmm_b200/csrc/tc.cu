@@ -1062,6 +1062,24 @@ tcaspmm_status tc_upload(const tcaspmm_csr &A, tcaspmm_dtype dt, Shard *sh)
     int per_sm = 0;
     if (e == cudaSuccess)
         e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tc_kernel<0>, NUM_THREADS, kSmemBytes);
+    // The occupancy query does not see the carveout preference set above (it
+    // answers 1 where ncu reports two resident CTAs), so the residency the SM's
+    // shared memory and register file allow is computed here as well, and the
+    // larger figure (at most 2) sizes the persistent grid.
+    if (e == cudaSuccess) {
+        int smem_sm = 0, reserved = 0, regs_sm = 0;
+        cudaFuncAttributes fa{};
+        if (cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, sh->device) ==
+                cudaSuccess &&
+            cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, sh->device) == cudaSuccess &&
+            cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, sh->device) == cudaSuccess &&
+            cudaFuncGetAttributes(&fa, tc_kernel<0>) == cudaSuccess && fa.numRegs > 0) {
+            const int by_smem = smem_sm / ((int)kSmemBytes + reserved);
+            const int by_regs = regs_sm / (NUM_THREADS * ((fa.numRegs + 7) / 8 * 8));
+            per_sm = std::max(per_sm, std::min(2, std::min(by_smem, by_regs)));
+        }
+        cudaGetLastError();
+    }
     sh->tc_ctas_per_sm = std::max(1, per_sm);
     return e == cudaSuccess ? TCASPMM_OK : cuda_fail(e, "tc kernel shared-memory opt-in");
 }
