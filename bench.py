@@ -131,6 +131,31 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
+def pin_to_gpu_numa_node(local_rank: int):
+    """Bind this process to the CPUs NVML reports as local to the GPU (its NUMA
+    node), so pinned host buffers are first touched there and the host side of the
+    copies runs next to the GPU's PCIe root.  Only this process's CPU affinity
+    changes; returns the previous affinity (to restore), or None."""
+    try:
+        import pynvml
+
+        before = os.sched_getaffinity(0)
+        pynvml.nvmlInit()
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        entry = vis.split(",")[local_rank].strip() if vis else str(local_rank)
+        h = (pynvml.nvmlDeviceGetHandleByIndex(int(entry)) if entry.isdigit()
+             else pynvml.nvmlDeviceGetHandleByUUID(entry))
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, (os.cpu_count() + 63) // 64)
+        cpus = {w * 64 + b for w, word in enumerate(words) for b in range(64) if (word >> b) & 1}
+        cpus &= before
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return before
+    except Exception:  # no NVML or no affinity information: leave the process as it is
+        return None
+
+
 def algorithmic_bytes(M, K, nnz, N, elem):
     return (M + 1) * 4 + nnz * (4 + elem) + K * N * elem + M * N * 4
 
@@ -329,6 +354,8 @@ def main():
     ap.add_argument("--split", default="columns", choices=["columns", "rows", "2d"],
                     help="multi-GPU partition: column blocks of B/C (A replicated), row blocks of A/C "
                          "(B replicated), or a 2-D grid of both (--grid)")
+    ap.add_argument("--numa", type=int, default=1, choices=[0, 1],
+                    help="1: bind each rank to its GPU's local CPUs (pinned buffers on that NUMA node)")
     ap.add_argument("--launch", default="graph", choices=["graph", "eager"],
                     help="timed step: replay a CUDA graph of the plan's launches, or call execute directly")
     ap.add_argument("--grid", default=None,
@@ -350,6 +377,7 @@ def main():
     if world != args.gpus:
         print(f"bench: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
     torch.cuda.set_device(local)
+    affinity_before = pin_to_gpu_numa_node(local) if args.numa else None
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
@@ -609,6 +637,8 @@ def main():
 
     # ---- CPU baseline (rank 0, N=1 only) ----
     cpu = None
+    if affinity_before is not None:
+        os.sched_setaffinity(0, affinity_before)  # the CPU baseline uses every host core
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle
 
@@ -641,6 +671,7 @@ def main():
                        else "inputs larger than L2 (126 MB)",
                        "launch": "CUDA graph of the plan's launches" if graph is not None
                        else "direct C-ABI execute per step",
+                       "host": "bound to the GPU's local CPUs" if affinity_before is not None else "unbound",
                        "preprocess_ms": round(pst["preprocess_ms"], 3), "upload_ms": round(pst["upload_ms"], 3),
                        "tc_windows": pst["tc_windows"], "residue_segments": pst["residue_segments"],
                        **({"epilogue": "C = relu(row_scale * (A B) + bias) stored as bf16"} if args.epilogue
