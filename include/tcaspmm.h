@@ -194,9 +194,10 @@ tcaspmm_status tcaspmm_partition_rows(const tcaspmm_csr *A, int parts, int64_t *
  *   TCASPMM_HUB_WINDOWS=0      1: long rows grouped by length into gathered
  *                              tensor-core windows
  *   TCASPMM_SPLIT_TILES=128    tiles per work item of a gathered window
+ *   TCASPMM_WINDOW_PARTS=1     parts per consecutive tensor-core window
  * Values are clamped (BUDGET_MAX to [16, 2^20], BUDGET_MIN to [1, 2^20],
  * WARPS_PER_SM to [1, 1024], DISABLE_TC and HUB_WINDOWS to [0, 1], SPLIT_TILES
- * to [1, 4096]); a value that is not a whole
+ * to [1, 4096], WINDOW_PARTS to [1, 64]); a value that is not a whole
  * number falls back to the default.  The results stay within the same
  * tolerances whatever these are; long rows may be summed in a different order. */
 

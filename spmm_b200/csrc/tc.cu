@@ -535,7 +535,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
                     for (int q = ptid; q < n * (G::TILE_VAL / 16); q += PTHREADS)
                         cp_async16(panel + PANEL_BYTES + q * 16, vsrc + q * 16, 16u);
                     cp_async_commit();
-                    ++npend;
+                    if (npend++ == 0) g_pend = g;  // the oldest pending stage is this one
                     if (npend == CP_DEPTH) release_oldest(CP_DEPTH - 1);
                 }
                 // Before a TMA task (or the end) every pending stage is released.
@@ -966,18 +966,22 @@ tcaspmm_status tc_upload(const tcaspmm_csr &A, tcaspmm_dtype dt, Shard *sh)
     std::vector<Task> tasks;
     int32_t groups = 0, slots = 0;
     const int split = (int)env_int("TCASPMM_SPLIT_TILES", SPLIT_TILES, 1, 4096);
+    // Consecutive windows stay whole unless TCASPMM_WINDOW_PARTS (clamped to
+    // [1, 64]) asks for that many parts of their tile chain (at most one per
+    // stage of tiles); a part of a consecutive column run starts 16 t0 columns in.
+    const int consec_parts = (int)env_int("TCASPMM_WINDOW_PARTS", 1, 1, 64);
     for (const Int4 &w : T.windows) {
-        // Consecutive windows stay whole: one CTA runs a window's tile chain (at
-        // most 256 tiles).  Cutting C1's windows in two to fill all CTA slots
-        // measured slower (16.3 against 12.3 us per step).
-        const int parts = w.x >= 0 ? 1 : (w.z + split - 1) / split;
+        const int parts = w.x >= 0 ? std::max(1, std::min(consec_parts, (w.z + Geo<0>::TPS - 1) / Geo<0>::TPS))
+                                   : (w.z + split - 1) / split;
+        const int32_t dense = w.x >= 0 ? dense_run(w) : -1;
         if (parts == 1) {
-            tasks.push_back(Task{w, Int4{-1, 0, 1, 0}, w.x >= 0 ? dense_run(w) : -1});
+            tasks.push_back(Task{w, Int4{-1, 0, 1, 0}, dense});
             continue;
         }
         for (int q = 0; q < parts; q++) {
             const int32_t t0 = (int32_t)((int64_t)w.z * q / parts), t1 = (int32_t)((int64_t)w.z * (q + 1) / parts);
-            tasks.push_back(Task{Int4{w.x, w.y + t0, t1 - t0, w.w}, Int4{groups, q, parts, slots}, -1});
+            tasks.push_back(Task{Int4{w.x, w.y + t0, t1 - t0, w.w}, Int4{groups, q, parts, slots},
+                                 dense >= 0 ? dense + t0 * KT : -1});
         }
         groups++;
         slots += parts;

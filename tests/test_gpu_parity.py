@@ -438,3 +438,39 @@ def test_dense_window_whose_last_stage_runs_past_b(K):
     B = g.integers(-4, 5, (K, 128)).astype(np.float32)
     out, _ = run(Ai, B, "f16")
     np.testing.assert_array_equal(out, reference(Ai, B, "f16"))
+
+
+def test_cta_running_a_tma_window_then_a_gathered_one():
+    """More work items than resident CTAs, so each CTA runs several: the first 320
+    windows are one consecutive column run (tiles fetched by TMA boxes), the next 320
+    skip four columns (tiles gathered by cp.async).  Windows have equal tile counts, so
+    a CTA's first item is a TMA window and a later one a gathered one -- the hand-over
+    between the two producer forms, integer values bit-exact."""
+    g = np.random.default_rng(31)
+    K, nd = 256, 320 * 32
+    cols, rp = [], [0]
+    keep_cols = np.setdiff1d(np.arange(K), np.arange(100, 104))
+    for r in range(2 * nd):
+        c = np.arange(K) if r < nd else np.sort(g.choice(keep_cols, 150, replace=False))
+        if r >= nd and r % 32 == 0:
+            c = keep_cols  # the window's union: every column but 100-103
+        cols.append(c.astype(np.int32))
+        rp.append(rp[-1] + c.size)
+    col = np.concatenate(cols)
+    A = T.CSR(2 * nd, K, np.asarray(rp, np.int64), col, g.integers(-3, 4, col.size).astype(np.float32))
+    B = g.integers(-4, 5, (K, 128)).astype(np.float32)
+    out, st = run(A, B, "f16")
+    assert st["tc_windows"] == 640 and st["tc_ctas_per_sm"] * 148 < 640, st
+    np.testing.assert_array_equal(out, reference(A, B, "f16"))
+
+
+@pytest.mark.parametrize("parts", ["2", "3", "5", "8"])
+def test_consecutive_windows_cut_into_parts(parts, monkeypatch):
+    """Consecutive windows cut into parts of their tile chain (reduced in part order),
+    including parts that start 48 rows into a 64-row stage (K = 300, 5 parts) and a last
+    window that is not one column run, so CTAs mix TMA and cp.async work items."""
+    monkeypatch.setenv("TCASPMM_WINDOW_PARTS", parts)
+    _, st = check(T.gen_uniform(1000, 300, 0.4, 11), 72, "f16")
+    assert st["tc_tasks"] > st["tc_windows"] > 0
+    _, st = check(T.gen_uniform(2048, 512, 0.3, 0), 256, "f16")
+    assert st["tc_tasks"] == 64 * int(parts), st
