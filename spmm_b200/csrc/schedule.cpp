@@ -6,7 +6,9 @@
 // Here:
 //   * rows are grouped into windows of R rows; a window whose condensed tiles
 //     move fewer bytes than gathering its rows one nonzero at a time becomes a
-//     tensor-core window (16-bit dtypes only);
+//     tensor-core window (16-bit dtypes and TF32); optionally, rows left over
+//     that are long are grouped by length into further windows with row lists
+//     (the long-row half of workload_manager, src/our_spmm.cu:392-395);
 //   * every other row belongs to exactly one contiguous row range, and ranges
 //     carry about the same cost (nnz + per-row overhead) per warp;
 //   * a row longer than twice the per-warp budget is cut into segments whose
@@ -49,16 +51,26 @@ int64_t env_int(const char *name, int64_t dflt, int64_t lo, int64_t hi)
 }
 
 // The sorted union of the columns of `rows` (n of them) and their nonzero
-// count.  `marks` is a zeroed byte per column of A, left zeroed on return.
+// count.  Small groups sort their columns; a group of more than 8192 nonzeros
+// marks them in `marks` (one byte per column of A, allocated on first use and
+// left zeroed), which costs O(nonzeros) instead of a sort of all of them.
 static void column_union(const tcaspmm_csr &A, const int32_t *rows, int n, std::vector<uint8_t> &marks,
                          std::vector<int32_t> *cols_u, int64_t *nnz_w)
 {
     cols_u->clear();
     int64_t nz = 0;
+    for (int i = 0; i < n; i++) nz += A.row_ptr[rows[i] + 1] - A.row_ptr[rows[i]];
+    *nnz_w = nz;
+    if (nz <= 8192) {
+        for (int i = 0; i < n; i++)
+            cols_u->insert(cols_u->end(), A.col_idx + A.row_ptr[rows[i]], A.col_idx + A.row_ptr[rows[i] + 1]);
+        std::sort(cols_u->begin(), cols_u->end());
+        cols_u->erase(std::unique(cols_u->begin(), cols_u->end()), cols_u->end());
+        return;
+    }
+    if (marks.empty()) marks.assign((size_t)A.ncol, 0);
     for (int i = 0; i < n; i++) {
-        const int64_t b = A.row_ptr[rows[i]], e = A.row_ptr[rows[i] + 1];
-        nz += e - b;
-        for (int64_t j = b; j < e; j++) {
+        for (int64_t j = A.row_ptr[rows[i]]; j < A.row_ptr[rows[i] + 1]; j++) {
             const int32_t c = A.col_idx[j];
             if (!marks[c]) {
                 marks[c] = 1;
@@ -67,7 +79,6 @@ static void column_union(const tcaspmm_csr &A, const int32_t *rows, int n, std::
         }
     }
     for (int32_t c : *cols_u) marks[c] = 0;
-    *nnz_w = nz;
     std::sort(cols_u->begin(), cols_u->end());
 }
 
@@ -123,7 +134,7 @@ tcaspmm_status build_schedule(const tcaspmm_csr &A, int64_t ncols, tcaspmm_dtype
                        env_int("TCASPMM_DISABLE_TC", 0, 0, 1) == 0;
     if (tc_ok) {
         const int nth = omp_get_max_threads();
-        std::vector<std::vector<uint8_t>> marks(nth, std::vector<uint8_t>((size_t)A.ncol, 0));
+        std::vector<std::vector<uint8_t>> marks((size_t)nth);  // per thread, allocated when a large group needs it
         // (1) Consecutive windows: blocks of R rows whose condensed tiles move fewer
         // bytes, are at least 1/8 dense and have at most 256 tiles (one CTA runs a
         // window's whole tile chain).  Evaluated in parallel, appended in order.
