@@ -28,9 +28,9 @@
 //
 // Warp roles: warps 0-3 epilogue (tcgen05.ld of TMEM lanes 32w..32w+31 ->
 // coalesced fp32 C rows), warp 4 TMEM allocation + MMA issue (one thread),
-// warp 5 producer on an 8-stage mbarrier ring, B-row indices staged in shared
-// memory by a coalesced warp load.  Two TMEM accumulators let the epilogue of
-// one unit overlap the MMAs of the next.
+// warps 5-7 producers on a 4-stage mbarrier ring (TMA stages round-robin from one
+// lane each, cp.async stages by all three warps together).  Two TMEM
+// accumulators let the epilogue of one work item overlap the MMAs of the next.
 //
 // Work items ("tasks") are windows or, for the gathered windows of long rows
 // (rows grouped by length, any row indices), consecutive parts of a window's
