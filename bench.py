@@ -384,7 +384,8 @@ def run_reference(args, wl):
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
     value = 2.0 * sample_nnz * N / t / 1e9
-    sample = (f"every {stride}th row ({rows.shape[0]} rows, {sample_nnz} nnz) per step; "
+    which = "all rows" if stride == 1 else f"every {stride}th row"
+    sample = (f"{which} ({rows.shape[0]} rows, {sample_nnz} nnz) per step; "
               f"full pass {t_full:.2f} s")
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",

@@ -195,9 +195,13 @@ tcaspmm_status tcaspmm_partition_rows(const tcaspmm_csr *A, int parts, int64_t *
  *                              tensor-core windows
  *   TCASPMM_SPLIT_TILES=128    tiles per work item of a gathered window
  *   TCASPMM_WINDOW_PARTS=1     parts per consecutive tensor-core window
+ *   TCASPMM_GATHER_TMA=1       0: gathered 16-bit tiles fetched by cp.async from
+ *                              all producer threads instead of TMA gather4
+ *   TCASPMM_DENSE_RUNS=1       0: windows whose columns are one consecutive run
+ *                              fetched through tile indices like gathered ones
  * Values are clamped (BUDGET_MAX to [16, 2^20], BUDGET_MIN to [1, 2^20],
- * WARPS_PER_SM to [1, 1024], DISABLE_TC and HUB_WINDOWS to [0, 1], SPLIT_TILES
- * to [1, 4096], WINDOW_PARTS to [1, 64]); a value that is not a whole
+ * WARPS_PER_SM to [1, 1024], DISABLE_TC, HUB_WINDOWS, GATHER_TMA and DENSE_RUNS
+ * to [0, 1], SPLIT_TILES to [1, 4096], WINDOW_PARTS to [1, 64]); a value that is not a whole
  * number falls back to the default.  The results stay within the same
  * tolerances whatever these are; long rows may be summed in a different order. */
 

@@ -65,8 +65,10 @@ constexpr int R = 32;            // window rows = MMA N
 constexpr int KT = 16;           // condensed columns per tile
 constexpr int MB = 128;          // output columns per unit = MMA M
 constexpr int STAGES = 4;        // pipeline stages of 20 KB
-constexpr int IDX_TILES = 16;    // tile column indices staged per refill (a multiple of every TPS); 16 keeps
-                                 // the shared memory of a CTA low enough for two CTAs per SM
+constexpr int IDX_TILES = 16;    // tile column indices staged per refill (a multiple of every TPS), two
+                                 // buffers a producer warp; 16 keeps a CTA's shared memory low enough for
+                                 // two CTAs per SM
+constexpr int IDX_INTS = IDX_TILES * KT;  // ints of one index buffer
 constexpr int PANEL_BYTES = 16384;                     // B panel per stage (any element type)
 constexpr int STAGE_BYTES = PANEL_BYTES + 4096;        // + the stage's value tiles
 
@@ -109,11 +111,10 @@ constexpr int PTHREADS = NPROD * 32;
 constexpr int ROW_STEP = PTHREADS / 16;                     // B rows a cp.async pass covers (16 threads a row)
 constexpr int ROW_PASSES = (64 + ROW_STEP - 1) / ROW_STEP;  // passes over a stage's 64 rows
 static_assert(PTHREADS % 16 == 0, "a B row slice is copied by 16 threads");
-// cp.async stages in flight per producer thread (at most STAGES: a thread
-// releases its oldest pending stage right after issuing a new one, before it waits
-// for the next slot).  Three measured faster than four (C3 f16 with gathered
-// windows 1.62 against 1.74 ms).
-constexpr int CP_DEPTH = 3;
+static_assert(2 * ROW_PASSES <= 32, "a producer warp's lanes hold the indices of its rows of a stage");
+// Stages ahead at which a cp.async producer loads B-row indices (a stage lasts
+// ~0.4 us, an index load from HBM up to ~1 us).
+constexpr int IDX_AHEAD = 3;
 constexpr int NUM_THREADS = 160 + 32 * NPROD;
 constexpr int CBUF_BYTES = 4 * 32 * 32 * 4;  // C staging: a 32 x 32 fp32 tile per epilogue warp
 constexpr int EPI_THREADS = 128;
@@ -125,7 +126,8 @@ struct TcParams {
     const int32_t *rows;     // row lists of the gathered windows
     float *partials;         // [slot][column block][epilogue warp][32 x 32] partial tiles of split windows
     unsigned int *counters;  // [split window][column block][epilogue warp], zero between launches
-    const int32_t *dense_c0; // per task: first column when its columns are one consecutive run, else -1
+    const int32_t *dense_c0; // per task: first column when its columns are one consecutive run; else
+                             // -2 (tiles fetched by TMA gather4) or -1 (16-bit tiles fetched by cp.async)
     const int32_t *tile_cols;
     const uint8_t *tile_vals;  // per tile: the value tile's shared-memory image
     const void *B;
@@ -205,18 +207,12 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32
 {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-// Wait until at most n of this thread's cp.async groups are pending (n < CP_DEPTH).
-__device__ __forceinline__ void cp_async_wait(int n)
+// Arrive on the barrier once every cp.async this thread issued so far has landed;
+// the arrival counts against the barrier's expected count (.noinc), so a thread
+// never blocks on its own copies.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar)
 {
-    if (n <= 0)
-        asm volatile("cp.async.wait_group 0;" ::: "memory");
-    else if (n == 1)
-        asm volatile("cp.async.wait_group 1;" ::: "memory");
-    else if (n == 2)
-        asm volatile("cp.async.wait_group 2;" ::: "memory");
-    else
-        asm volatile("cp.async.wait_group 3;" ::: "memory");
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
@@ -384,8 +380,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     // 1024-byte aligned stage ring, then the index buffer and the barriers.
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *cbuf = smem + STAGES * STAGE_BYTES;                             // [4 warps][32 rows][32 columns]
-    int32_t *idxbuf = (int32_t *)(smem + STAGES * STAGE_BYTES + CBUF_BYTES);  // [NPROD][IDX_TILES][KT]
-    uint64_t *bars = (uint64_t *)(smem + STAGES * STAGE_BYTES + CBUF_BYTES + NPROD * IDX_TILES * KT * 4);
+    int32_t *idxbuf = (int32_t *)(smem + STAGES * STAGE_BYTES + CBUF_BYTES);  // [NPROD][2][IDX_TILES][KT]
+    uint64_t *bars = (uint64_t *)(smem + STAGES * STAGE_BYTES + CBUF_BYTES + NPROD * 2 * IDX_INTS * 4);
     uint64_t *full = bars;                  // [STAGES] producer -> MMA
     uint64_t *empty = bars + STAGES;        // [STAGES] MMA -> producer
     uint64_t *accf = bars + 2 * STAGES;     // [2] MMA -> epilogue
@@ -437,36 +433,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     if (warp >= 5) {
         // ------------------------------ producers ------------------------------
         // Warps 5 .. 5 + NPROD - 1 walk the same stage sequence.
-        //  * TMA stages (windows whose columns are one consecutive run, and the
-        //    tf32 gathers): warp 5 + i fills the stages g with g % NPROD == i from
+        //  * TMA stages (windows whose columns are one consecutive run, and
+        //    gathered tiles): warp 5 + i fills the stages g with g % NPROD == i from
         //    one lane -- one 64 x 64 box per column piece when the stage's B rows
         //    are consecutive, else per tile a 64 x 16 box or four gather4 loads,
         //    plus one bulk copy of the stage's value tiles -- and arrives for all
         //    producer threads.
-        //  * cp.async stages (gathered 16-bit tiles): all PTHREADS threads copy
+        //  * cp.async stages (gathered 16-bit tiles under TCASPMM_GATHER_TMA=0):
+        //    all PTHREADS threads copy
         //    the stage's B row slices (16 bytes each, coalesced per row) straight
         //    into the 128-byte-swizzled panel layout, and the value tiles; each
-        //    thread keeps up to CP_DEPTH stages in flight and arrives on a stage's
-        //    full barrier once its own copies of that stage landed (after a proxy
-        //    fence, so the tensor cores see them).
+        //    thread's arrival on the stage's full barrier is triggered by the
+        //    landing of its copies, so every free slot of the ring is in flight
+        //    (the MMA issuer fences the proxies before its tensor cores read them).
         const int pw = warp - 5;
         const int ptid = tid - 160;  // 0 .. PTHREADS - 1
-        int32_t *myidx = idxbuf + pw * IDX_TILES * KT;
+        int32_t *const mybufs = idxbuf + pw * 2 * IDX_INTS;  // this warp's two index buffers
         uint32_t g = 0;  // stages of this CTA (issued by this warp or the other producers)
         bool ok = true;
-        uint32_t g_pend = 0;  // oldest of this thread's cp.async stages not yet arrived on
-        int npend = 0;
         uint32_t tma_mine = 0;  // bit s: this lane issued the TMA copies of the stage now in slot s
-        auto release_oldest = [&](int keep) {
-            // This thread's copies of its oldest pending stage have landed once at
-            // most `keep` groups remain; make them visible to the async proxy and
-            // count this thread in.
-            cp_async_wait(keep);
-            fence_proxy_async();
-            mbar_arrive(smem_u32(&full[g_pend % STAGES]));
-            ++g_pend;
-            --npend;
-        };
         const void *tm_g = &maps.gather, *tm_16 = &maps.box16, *tm_64 = &maps.box64;
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(tm_g) : "memory");
@@ -483,34 +468,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
             const int n0 = (u % p.nfb) * MB;
             const int nst = (w.z + G::TPS - 1) / G::TPS;  // stages of this unit (w.z >= 1)
             const int rot = win % nst;
-            if (c0 < 0 && FMT != 2) {
+            if (c0 == -1 && FMT != 2) {
                 // Gathered 16-bit tiles through cp.async: thread ptid copies the
-                // 16-byte chunk cc = ptid % 16 of B rows k = ptid / 16 + ROW_STEP i.  The
-                // B-row indices of the next stage are loaded one stage ahead, so
-                // issuing a stage never waits on an index load.
+                // 16-byte chunk cc = ptid % 16 of B rows k = ptid / 16 + ROW_STEP i.
+                // The B-row indices are loaded IDX_AHEAD stages ahead, one per lane:
+                // lane j < 2 ROW_PASSES of producer warp pw holds the index of the
+                // stage's row 2 pw + j % 2 + ROW_STEP (j / 2), which lanes
+                // 16 (j % 2) .. + 15 of the warp copy in pass j / 2, and hands it to
+                // them by a shuffle.  So issuing a stage never waits on an index load.
                 const int cc = ptid & 15, pc = cc >> 3, c = cc & 7;
                 const int col = n0 + cc * 8;  // first of the chunk's 8 columns
                 const bool colok = col < p.ncols;
-                int nxt[ROW_PASSES];  // B rows of the next stage's rows k = ptid / 16 + ROW_STEP i
-                auto load_rows = [&](int k) {
+                const int jr = 2 * pw + (lane & 1) + ROW_STEP * (lane >> 1);
+                auto load_row = [&](int k) -> int {
+                    if (k >= nst || lane >= 2 * ROW_PASSES) return 0;
                     const int t = stage_at(k, rot, nst) * G::TPS;
                     const int rows = min(G::TPS, w.z - t) * KT;
-                    const int32_t *tcols = p.tile_cols + ((long long)w.y + t) * KT;
-#pragma unroll
-                    for (int i = 0; i < ROW_PASSES; ++i) {
-                        const int kr = (ptid >> 4) + ROW_STEP * i;
-                        nxt[i] = kr < rows ? __ldg(tcols + kr) : 0;
-                    }
+                    return jr < rows ? __ldg(p.tile_cols + ((long long)w.y + t) * KT + jr) : 0;
                 };
-                load_rows(0);
+                static_assert(IDX_AHEAD == 3, "the index ring below holds three stages");
+                int ia = load_row(0), ib = load_row(1), ic = load_row(2);
                 for (int k = 0; k < nst; ++k, ++g) {
                     const int t = stage_at(k, rot, nst) * G::TPS;
                     const int s = g % STAGES;
                     const int n = min(G::TPS, w.z - t);
-                    int brow[ROW_PASSES];
-#pragma unroll
-                    for (int i = 0; i < ROW_PASSES; ++i) brow[i] = nxt[i];
-                    if (k + 1 < nst) load_rows(k + 1);
+                    const int cur = ia;
+                    ia = ib;
+                    ib = ic;
+                    ic = load_row(k + IDX_AHEAD);
                     // Abort decisions stay warp-uniform (the lanes of a producer warp
                     // walk the same stages).
                     ok = __all_sync(0xffffffffu, wait_bounded(smem_u32(&empty[s]), ((g / STAGES) & 1) ^ 1,
@@ -523,10 +508,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
 #pragma unroll
                     for (int i = 0; i < ROW_PASSES; ++i) {
                         const int kr = (ptid >> 4) + ROW_STEP * i;
+                        const int brow = __shfl_sync(0xffffffffu, cur, 2 * i + (lane >> 4));
                         if (kr < rows) {
                             const uint32_t dst = panel + pc * G::PIECE + (kr >> 3) * 1024 + (kr & 7) * 128 +
                                                  ((c ^ (kr & 7)) << 4);
-                            const char *src = colok ? Bbytes + (long long)brow[i] * pitch + (long long)col * G::ES
+                            const char *src = colok ? Bbytes + (long long)brow * pitch + (long long)col * G::ES
                                                     : Bbytes;
                             cp_async16(dst, src, colok ? 16u : 0u);
                         }
@@ -534,15 +520,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
                     const uint8_t *vsrc = p.tile_vals + ((long long)w.y + t) * G::TILE_VAL;
                     for (int q = ptid; q < n * (G::TILE_VAL / 16); q += PTHREADS)
                         cp_async16(panel + PANEL_BYTES + q * 16, vsrc + q * 16, 16u);
-                    cp_async_commit();
-                    if (npend++ == 0) g_pend = g;  // the oldest pending stage is this one
-                    if (npend == CP_DEPTH) release_oldest(CP_DEPTH - 1);
+                    cp_async_arrive_noinc(smem_u32(&full[s]));
                 }
-                // Before a TMA task (or the end) every pending stage is released.
-                const int un = u + gridDim.x;
-                const bool next_cp = ok && un < p.n_units && p.dense_c0[un / p.nfb] < 0;
-                if (!next_cp)
-                    while (npend > 0) release_oldest(npend - 1);
                 continue;
             }
             if (c0 >= 0) {
@@ -582,16 +561,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
                 }
                 continue;
             }
-            int chunk = -1;  // IDX_TILES-tile chunk whose indices are staged
+            // Tile indices in IDX_TILES-tile chunks, two buffers a warp: when the
+            // stages reach a new chunk, the chunk after it in this task's stage
+            // order is fetched by cp.async into the other buffer, so its load
+            // overlaps a chunk's worth of stages (a task's first chunk is waited for).
+            constexpr int SPC = IDX_TILES / G::TPS;  // stages a chunk
+            int chunk = -1, pre = -1, cur = 0;       // staged chunk, chunk in flight, buffer of `chunk`
+            const int32_t *myidx = mybufs;
+            auto fetch = [&](int ch, int32_t *dst) {
+                const int t0 = ch * IDX_TILES, n16 = min(IDX_TILES, w.z - t0) * (KT / 4);
+                const int32_t *src = p.tile_cols + ((long long)w.y + t0) * KT;
+                for (int q = lane; q < n16; q += 32) cp_async16(smem_u32(dst + 4 * q), src + 4 * q, 16u);
+            };
             for (int k = 0; ok && k < nst; ++k, ++g) {
-                const int t = stage_at(k, rot, nst) * G::TPS;  // first tile of the stage
+                const int sk = stage_at(k, rot, nst);
+                const int t = sk * G::TPS;  // first tile of the stage
                 if (t / IDX_TILES != chunk) {
                     chunk = t / IDX_TILES;
-                    const int t0 = chunk * IDX_TILES, nt = min(IDX_TILES, w.z - t0);
                     __syncwarp();  // previous indices consumed
-                    for (int q = lane; q < nt * KT; q += 32)
-                        myidx[q] = __ldg(p.tile_cols + ((long long)w.y + t0) * KT + q);
+                    if (chunk == pre) {
+                        cur ^= 1;
+                    } else {
+                        // Not prefetched: any copy still landing in a buffer ends first.
+                        asm volatile("cp.async.wait_all;" ::: "memory");
+                        fetch(chunk, mybufs + cur * IDX_INTS);
+                    }
+                    asm volatile("cp.async.wait_all;" ::: "memory");
                     __syncwarp();  // indices visible to the warp
+                    myidx = mybufs + cur * IDX_INTS;
+                    // This chunk's run of stages ends at its last stage or the task's;
+                    // the stage after the run starts the next chunk.
+                    const int k2 = k + min((chunk + 1) * SPC, nst) - sk;
+                    pre = -1;
+                    if (k2 < nst) {
+                        pre = stage_at(k2, rot, nst) / SPC;
+                        fetch(pre, mybufs + (cur ^ 1) * IDX_INTS);
+                    }
                 }
                 tma_mine &= ~(1u << (g % STAGES));
                 if ((int)(g % NPROD) != pw) continue;
@@ -656,11 +661,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
             constexpr uint32_t idesc = instr_desc<FMT>();
             uint32_t g = 0, i = 0;
             bool ok = true;
-            // Task descriptors are loaded one task ahead.
-            int4 wn = (int)blockIdx.x < p.n_units ? p.tasks[blockIdx.x / p.nfb] : make_int4(0, 0, 1, 0);
+            // Task descriptors (and whether the producers fill the task's stages
+            // through cp.async) are loaded one task ahead.
+            const bool first_ok = (int)blockIdx.x < p.n_units;
+            int4 wn = first_ok ? p.tasks[blockIdx.x / p.nfb] : make_int4(0, 0, 1, 0);
+            bool cpn = FMT != 2 && first_ok && p.dense_c0[blockIdx.x / p.nfb] == -1;
             for (int u = blockIdx.x; ok && u < p.n_units; u += gridDim.x, ++i) {
                 const int4 w = wn;
-                if (u + (int)gridDim.x < p.n_units) wn = p.tasks[(u + gridDim.x) / p.nfb];
+                const bool cp = cpn;
+                if (u + (int)gridDim.x < p.n_units) {
+                    wn = p.tasks[(u + gridDim.x) / p.nfb];
+                    cpn = FMT != 2 && p.dense_c0[(u + gridDim.x) / p.nfb] == -1;
+                }
                 const uint32_t a = i & 1;
                 if (!wait_bounded(smem_u32(&acce[a]), ((i >> 1) & 1) ^ 1, abort_flag, p.err, 2, p.wait_cycles)) break;
                 tc_fence_after();
@@ -678,6 +690,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
                         break;
                     }
                     tc_fence_after();
+                    if (cp) fence_proxy_async();  // cp.async (generic proxy) writes -> tensor-core reads
                     const uint32_t panel = smem_u32(smem + s * STAGE_BYTES);
                     for (int j = 0; j < n; ++j) {
 #pragma unroll
@@ -806,7 +819,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
 // Tail: 2 * STAGES + 5 mbarriers, the TMEM address and the abort flag.
 constexpr size_t kBarBytes = (2 * STAGES + 5) * 8 + 8;
 constexpr size_t kSmemBytes =
-    1024 + STAGES * STAGE_BYTES + CBUF_BYTES + NPROD * IDX_TILES * KT * 4 + (kBarBytes + 127) / 128 * 128;  // ~101 KB: two CTAs per SM
+    1024 + STAGES * STAGE_BYTES + CBUF_BYTES + NPROD * 2 * IDX_INTS * 4 + (kBarBytes + 127) / 128 * 128;  // ~104 KB: two CTAs per SM
 
 template <typename X>
 tcaspmm_status upload_vec(Shard *sh, X **dst, const std::vector<X> &v, const char *what)
@@ -970,10 +983,19 @@ tcaspmm_status tc_upload(const tcaspmm_csr &A, tcaspmm_dtype dt, Shard *sh)
     // [1, 64]) asks for that many parts of their tile chain (at most one per
     // stage of tiles); a part of a consecutive column run starts 16 t0 columns in.
     const int consec_parts = (int)env_int("TCASPMM_WINDOW_PARTS", 1, 1, 64);
+    // TCASPMM_DENSE_RUNS=0 sends consecutive column runs through the gathered
+    // path (tile indices, cp.async for 16-bit B) instead of TMA boxes.
+    const bool dense_runs = env_flag("TCASPMM_DENSE_RUNS", true);
+    // Gathered 16-bit tiles are fetched by TMA gather4 (as TF32 tiles are);
+    // TCASPMM_GATHER_TMA=0 fetches them by cp.async from all producer threads
+    // (measured slower: C2 at 80% sparsity 45 against 25 us, C3 gathered
+    // windows 1.64 against 1.53 ms).
+    const int32_t gathered = env_flag("TCASPMM_GATHER_TMA", true) ? -2 : -1;
     for (const Int4 &w : T.windows) {
         const int parts = w.x >= 0 ? std::max(1, std::min(consec_parts, (w.z + Geo<0>::TPS - 1) / Geo<0>::TPS))
                                    : (w.z + split - 1) / split;
-        const int32_t dense = w.x >= 0 ? dense_run(w) : -1;
+        const int32_t run = w.x >= 0 && dense_runs ? dense_run(w) : -1;
+        const int32_t dense = run >= 0 ? run : gathered;
         if (parts == 1) {
             tasks.push_back(Task{w, Int4{-1, 0, 1, 0}, dense});
             continue;
@@ -981,7 +1003,7 @@ tcaspmm_status tc_upload(const tcaspmm_csr &A, tcaspmm_dtype dt, Shard *sh)
         for (int q = 0; q < parts; q++) {
             const int32_t t0 = (int32_t)((int64_t)w.z * q / parts), t1 = (int32_t)((int64_t)w.z * (q + 1) / parts);
             tasks.push_back(Task{Int4{w.x, w.y + t0, t1 - t0, w.w}, Int4{groups, q, parts, slots},
-                                 dense >= 0 ? dense + t0 * KT : -1});
+                                 dense >= 0 ? dense + t0 * KT : dense});
         }
         groups++;
         slots += parts;

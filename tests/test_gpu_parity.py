@@ -339,11 +339,14 @@ def _window_union_matrix(unions, K, seed=21, drop=0.1):
     return T.CSR(32 * len(unions), K, np.asarray(rp, np.int64), np.concatenate(cols), np.concatenate(vals))
 
 
-def test_tensor_core_stage_shapes_bit_exact():
+@pytest.mark.parametrize("gather_tma", ["1", "0"])
+def test_tensor_core_stage_shapes_bit_exact(gather_tma, monkeypatch):
     """Every producer form: 64-row boxes, 16-row boxes, gather4 tiles, partial stages,
     index refills past 32 tiles, a padded last tile whose span looks like 16
     consecutive rows ({.., 40, 55, 55, ..}) but is not, and windows whose columns
-    are one consecutive run (loaded without tile indices, boxes reaching past K)."""
+    are one consecutive run (loaded without tile indices, boxes reaching past K);
+    gathered 16-bit tiles by TMA gather4 (default) and by cp.async."""
+    monkeypatch.setenv("TCASPMM_GATHER_TMA", gather_tma)
     K = 2048
     unions = [
         list(range(32)) + [40, 55],                                   # padded tile of span 15
@@ -364,6 +367,29 @@ def test_tensor_core_stage_shapes_bit_exact():
             np.testing.assert_array_equal(out, reference(A, B[:, :N], dt).astype(np.float32))
 
 
+@pytest.mark.parametrize("dt,gather_tma", [("f16", "1"), ("f16", "0"), ("tf32", "1")])
+def test_gathered_tile_index_chunks_bit_exact(dt, gather_tma, monkeypatch):
+    """Gathered tile chains long enough for many 16-tile index chunks, walked from a
+    rotated first stage (work items run by decreasing tile count, item i starting at
+    stage i mod its stages): chunk prefetches across the wrap from the last stage to
+    the first, chains that start inside a chunk and come back to it, and a one-chunk
+    chain that wraps within its chunk."""
+    monkeypatch.setenv("TCASPMM_GATHER_TMA", gather_tma)
+    K = 8192
+    unions = [
+        list(range(0, 200 * 32, 2)),      # 200 tiles (50 f16 stages), item 0: first stage 0
+        list(range(0, 12 * 48, 3)),       # 12 tiles, item 4: one chunk, starts at stage 1, wraps in it
+        list(range(1, 150 * 32, 2)),      # 150 tiles, item 1: starts one stage into its first chunk
+        list(range(7, 70 * 32 + 7, 2)),   # 70 tiles, item 2: starts two stages in
+        list(range(0, 17 * 32, 2)),       # 17 tiles, item 3: chunk 0 from stage 3, chunk 1, chunk 0 again
+    ]
+    A = _window_union_matrix(unions, K, seed=27)
+    B = np.round(T.gen_dense(K, 128, 6, "f32") * 4).astype(np.float32)
+    out, st = run(A, B, dt)
+    assert st["tc_windows"] == len(unions) and st["tc_nnz"] == st["nnz"], st
+    np.testing.assert_array_equal(out, reference(A, B, dt).astype(np.float32))
+
+
 # ---------------------------------------------------- gathered windows (long rows)
 @pytest.mark.parametrize("dt", ["f16", "bf16", "tf32"])
 @pytest.mark.parametrize("N", [128, 64, 256, 200])
@@ -379,9 +405,12 @@ def test_gathered_windows_of_long_rows(dt, N, split, monkeypatch):
     assert st["tc_gathered_windows"] > 0 and st["tc_tasks"] > st["tc_windows"], st
 
 
-def test_gathered_windows_integer_values_bit_exact(monkeypatch):
+@pytest.mark.parametrize("gather_tma", ["1", "0"])
+def test_gathered_windows_integer_values_bit_exact(gather_tma, monkeypatch):
     """Integer A and B small enough that every fp32 sum is exact: tiles, split parts
-    and the fixed-order reduction must reproduce the oracle bit for bit."""
+    and the fixed-order reduction must reproduce the oracle bit for bit (tiles fetched
+    by TMA gather4 and by cp.async)."""
+    monkeypatch.setenv("TCASPMM_GATHER_TMA", gather_tma)
     monkeypatch.setenv("TCASPMM_HUB_WINDOWS", "1")
     monkeypatch.setenv("TCASPMM_SPLIT_TILES", "5")
     A = T.gen_rmat(13, 120000, kind="gcn", seed=9)
@@ -440,12 +469,14 @@ def test_dense_window_whose_last_stage_runs_past_b(K):
     np.testing.assert_array_equal(out, reference(Ai, B, "f16"))
 
 
-def test_cta_running_a_tma_window_then_a_gathered_one():
+@pytest.mark.parametrize("gather_tma", ["1", "0"])
+def test_cta_running_a_tma_window_then_a_gathered_one(gather_tma, monkeypatch):
     """More work items than resident CTAs, so each CTA runs several: the first 320
     windows are one consecutive column run (tiles fetched by TMA boxes), the next 320
-    skip four columns (tiles gathered by cp.async).  Windows have equal tile counts, so
-    a CTA's first item is a TMA window and a later one a gathered one -- the hand-over
-    between the two producer forms, integer values bit-exact."""
+    skip four columns (tiles gathered by TMA gather4, or by cp.async).  Windows have
+    equal tile counts, so a CTA's first item is a TMA-box window and a later one a
+    gathered one -- the hand-over between producer forms, integer values bit-exact."""
+    monkeypatch.setenv("TCASPMM_GATHER_TMA", gather_tma)
     g = np.random.default_rng(31)
     K, nd = 256, 320 * 32
     cols, rp = [], [0]
