@@ -101,6 +101,7 @@ typedef struct tcaspmm_plan_stats {
     int64_t tc_gathered_windows; /* tc windows of long rows grouped by length (row lists) */
     int64_t tc_tasks;         /* tensor-core work items per column block (windows split by tiles) */
     int64_t tc_ctas_per_sm;   /* resident tensor-core CTAs per SM (the persistent grid is this x SMs) */
+    int64_t tc_side_stream;   /* 1: the tensor-core kernel runs beside the residue kernel on a side stream */
 } tcaspmm_plan_stats;
 
 /* ---------------------------------------------------------------- errors */
@@ -194,15 +195,22 @@ tcaspmm_status tcaspmm_partition_rows(const tcaspmm_csr *A, int parts, int64_t *
  *   TCASPMM_HUB_WINDOWS=0      1: long rows grouped by length into gathered
  *                              tensor-core windows
  *   TCASPMM_SPLIT_TILES=128    tiles per work item of a gathered window
- *   TCASPMM_WINDOW_PARTS=1     parts per consecutive tensor-core window
+ *   TCASPMM_WINDOW_PARTS=0     parts per consecutive tensor-core window (0: cut
+ *                              into parts of at least 4 stages only while the
+ *                              work items leave SMs without one)
  *   TCASPMM_GATHER_TMA=1       0: gathered 16-bit tiles fetched by cp.async from
  *                              all producer threads instead of TMA gather4
  *   TCASPMM_DENSE_RUNS=1       0: windows whose columns are one consecutive run
  *                              fetched through tile indices like gathered ones
+ *   TCASPMM_TC_DENSITY=32      a consecutive window needs at least 1/this of its
+ *                              tile entries nonzero
+ *   TCASPMM_OVERLAP=1          0: the tensor-core kernel never runs beside the
+ *                              residue kernel on a side stream
  * Values are clamped (BUDGET_MAX to [16, 2^20], BUDGET_MIN to [1, 2^20],
- * WARPS_PER_SM to [1, 1024], DISABLE_TC, HUB_WINDOWS, GATHER_TMA and DENSE_RUNS
- * to [0, 1], SPLIT_TILES to [1, 4096], WINDOW_PARTS to [1, 64]); a value that is not a whole
- * number falls back to the default.  The results stay within the same
+ * WARPS_PER_SM to [1, 1024], TC_DENSITY to [1, 1024], DISABLE_TC, HUB_WINDOWS,
+ * GATHER_TMA, DENSE_RUNS and OVERLAP to [0, 1], SPLIT_TILES to [1, 4096],
+ * WINDOW_PARTS to [0, 64]); a value that is not a whole number falls back to
+ * the default.  The results stay within the same
  * tolerances whatever these are; long rows may be summed in a different order. */
 
 /* One plan over num_gpus devices (devices[i], or 0..num_gpus-1 when NULL); the

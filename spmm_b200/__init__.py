@@ -100,7 +100,7 @@ class _Stats(C.Structure):
                 ("residue_row_warps", C.c_int64), ("residue_segments", C.c_int64), ("long_rows", C.c_int64),
                 ("preprocess_ms", C.c_double), ("upload_ms", C.c_double), ("device_bytes", C.c_int64),
                 ("algorithmic_bytes", C.c_int64), ("tc_gathered_windows", C.c_int64), ("tc_tasks", C.c_int64),
-                ("tc_ctas_per_sm", C.c_int64)]
+                ("tc_ctas_per_sm", C.c_int64), ("tc_side_stream", C.c_int64)]
 
     def to_dict(self) -> dict:
         return {name: getattr(self, name) for name, _ in self._fields_}

@@ -154,6 +154,21 @@ tcaspmm_status build_shard(const tcaspmm_csr &Afull, tcaspmm_dtype dt, int devic
     e = cudaMemset(sh->err, 0, 6 * sizeof(int));
     if (e != cudaSuccess) return cuda_fail(e, "zero error word");
     if ((s = tc_upload(A, dt, sh)) != TCASPMM_OK) return s;
+    // Both kernels in one launch: when the tensor-core work items leave CTA slots
+    // free, the tensor-core kernel runs on a side stream beside the residue rows
+    // instead of before them (a few long tile chains no longer add their latency
+    // to the residue kernel's); when they fill every slot, the two kernels would
+    // only contend, and run one after the other.  TCASPMM_OVERLAP=0 never forks.
+    const int64_t tc_units = (int64_t)sh->n_tasks * ((ncols + 127) / 128);
+    if (sh->n_tasks > 0 && sh->n_ranges + sh->n_segs > 0 && tc_units < (int64_t)sh->tc_ctas_per_sm * sh->num_sms &&
+        env_flag("TCASPMM_OVERLAP", true)) {
+        int least = 0, greatest = 0;
+        e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
+        if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&sh->side, cudaStreamNonBlocking, greatest);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sh->ev_fork, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sh->ev_join, cudaEventDisableTiming);
+        if (e != cudaSuccess) return cuda_fail(e, "side stream");
+    }
     e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return cuda_fail(e, "plan upload");
     return TCASPMM_OK;
@@ -216,8 +231,13 @@ tcaspmm_status launch_residue(const Shard &sh, tcaspmm_dtype dt, const void *dB,
 
 void free_shard(Shard &sh)
 {
-    if (sh.allocs.empty()) return;
+    if (sh.allocs.empty() && !sh.side && !sh.ev_fork && !sh.ev_join) return;
     DeviceGuard g(sh.device);
+    if (sh.ev_join) cudaEventDestroy(sh.ev_join);
+    if (sh.ev_fork) cudaEventDestroy(sh.ev_fork);
+    if (sh.side) cudaStreamDestroy(sh.side);
+    sh.ev_join = sh.ev_fork = nullptr;
+    sh.side = nullptr;
     for (void *p : sh.allocs) cudaFree(p);
     sh.allocs.clear();
 }
@@ -277,6 +297,7 @@ static tcaspmm_status create_common(const tcaspmm_csr *A, int64_t N, tcaspmm_dty
         st.tc_gathered_windows += Si.tc.gathered;
         st.tc_tasks += P->shards[i]->n_tasks;
         if (P->shards[i]->n_tasks) st.tc_ctas_per_sm = P->shards[i]->tc_ctas_per_sm;
+        if (P->shards[i]->side) st.tc_side_stream = 1;
         st.tc_tiles += Si.tc.KT ? (int64_t)Si.tc.tile_cols.size() / Si.tc.KT : 0;
         st.tc_nnz += Si.tc.nnz;
         st.residue_nnz += Si.res.nnz;
@@ -499,6 +520,23 @@ tcaspmm_status tcaspmm_execute_ex(tcaspmm_plan *plan, const void *const *dB, con
         cudaStream_t st = streams ? (cudaStream_t)streams[i] : (cudaStream_t)0;
         DeviceGuard g(sh.device);
         const Epilogue *epp = epilogues ? &ep : nullptr;
+        if (sh.side) {
+            // Fork: the tensor-core kernel on the side stream, the residue kernel on
+            // the caller's; joined before anything later on the caller's stream.
+            // The join is recorded even when a launch failed, so a stream capture
+            // never holds an unjoined fork.
+            cudaError_t e = cudaEventRecord(sh.ev_fork, st);
+            if (e == cudaSuccess) e = cudaStreamWaitEvent(sh.side, sh.ev_fork, 0);
+            if (e != cudaSuccess) return cuda_fail(e, "fork to the side stream");
+            const tcaspmm_status s_tc = launch_tc(sh, plan->dt, dB[i], ldb[i], dC[i], ldc[i], epp, sh.side);
+            const tcaspmm_status s_res = launch_residue(sh, plan->dt, dB[i], ldb[i], dC[i], ldc[i], epp, st);
+            e = cudaEventRecord(sh.ev_join, sh.side);
+            if (e == cudaSuccess) e = cudaStreamWaitEvent(st, sh.ev_join, 0);
+            if (s_tc != TCASPMM_OK) return s_tc;
+            if (s_res != TCASPMM_OK) return s_res;
+            if (e != cudaSuccess) return cuda_fail(e, "join from the side stream");
+            continue;
+        }
         tcaspmm_status s = launch_tc(sh, plan->dt, dB[i], ldb[i], dC[i], ldc[i], epp, st);
         if (s != TCASPMM_OK) return s;
         s = launch_residue(sh, plan->dt, dB[i], ldb[i], dC[i], ldc[i], epp, st);

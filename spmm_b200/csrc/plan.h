@@ -63,6 +63,12 @@ struct Shard {
     mutable int cmap_out = 0;
 
     int *err = nullptr;  // device error words: codes of bounded waits that ran out, and where the first did
+
+    // When a shard has both tensor-core tasks and residue work, the tensor-core
+    // kernel runs on this (high-priority) stream beside the residue kernel on the
+    // caller's stream, forked and joined by the two events.
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
 };
 
 // Fused output epilogue of one launch (tcaspmm_epilogue after validation):

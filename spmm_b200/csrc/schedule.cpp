@@ -136,9 +136,13 @@ tcaspmm_status build_schedule(const tcaspmm_csr &A, int64_t ncols, tcaspmm_dtype
         const int nth = omp_get_max_threads();
         std::vector<std::vector<uint8_t>> marks((size_t)nth);  // per thread, allocated when a large group needs it
         // (1) Consecutive windows: blocks of R rows whose condensed tiles move fewer
-        // bytes, are at least 1/8 dense and have at most 256 tiles (one CTA runs a
-        // window's whole tile chain).  Evaluated in parallel, appended in order.
+        // bytes, are at least 1/32 dense (TCASPMM_TC_DENSITY) and have at most 256
+        // tiles.  Evaluated in parallel, appended in order.  The density floor was
+        // measured over the pruned-weight sweep (3 shapes x 4 sparsities x 2
+        // structures x N = 128 / 512, f16): 1/32 within 1% of the best floor per
+        // case on geometric mean (1/16: 12%, 1/8: 25%).
         const int64_t nwin = (M + R - 1) / R;
+        const double density_div = (double)env_int("TCASPMM_TC_DENSITY", 32, 1, 1024);
         std::vector<std::vector<int32_t>> ok_cols((size_t)nwin);
         std::vector<int64_t> ok_nz((size_t)nwin, -1);
 #pragma omp parallel for schedule(dynamic, 64)
@@ -151,7 +155,7 @@ tcaspmm_status build_schedule(const tcaspmm_csr &A, int64_t ncols, tcaspmm_dtype
             int64_t nz;
             column_union(A, rows, n, marks[omp_get_thread_num()], &cols_u, &nz);
             const int64_t ntiles = ((int64_t)cols_u.size() + S.tc.KT - 1) / S.tc.KT;
-            if (nz == 0 || ntiles > 256 || (double)nz < (double)ntiles * S.tc.KT * n / 8.0 ||
+            if (nz == 0 || ntiles > 256 || (double)nz < (double)ntiles * S.tc.KT * n / density_div ||
                 !tiles_pay((int64_t)cols_u.size(), nz, S.tc.KT, R, ncols, elem))
                 continue;
             ok_cols[w] = std::move(cols_u);

@@ -946,6 +946,9 @@ bool tc_supported()
 // over many CTAs while each part still amortises its epilogue.  The tuning
 // variable TCASPMM_SPLIT_TILES (clamped to [1, 4096]) overrides it.
 constexpr int SPLIT_TILES = 128;
+// Fewest pipeline stages in a part of a consecutive window cut for idle SMs: a
+// part's epilogue and reduction cost about a stage.
+constexpr int MIN_PART_STAGES = 4;
 
 tcaspmm_status tc_upload(const tcaspmm_csr &A, tcaspmm_dtype dt, Shard *sh)
 {
@@ -979,10 +982,19 @@ tcaspmm_status tc_upload(const tcaspmm_csr &A, tcaspmm_dtype dt, Shard *sh)
     std::vector<Task> tasks;
     int32_t groups = 0, slots = 0;
     const int split = (int)env_int("TCASPMM_SPLIT_TILES", SPLIT_TILES, 1, 4096);
-    // Consecutive windows stay whole unless TCASPMM_WINDOW_PARTS (clamped to
-    // [1, 64]) asks for that many parts of their tile chain (at most one per
-    // stage of tiles); a part of a consecutive column run starts 16 t0 columns in.
-    const int consec_parts = (int)env_int("TCASPMM_WINDOW_PARTS", 1, 1, 64);
+    // Consecutive windows: when their work items (with the gathered windows'
+    // parts, per column block) leave SMs without one, each tile chain is cut into
+    // up to SMs / items parts of at least MIN_PART_STAGES stages, so a few long
+    // chains spread over idle SMs; otherwise they stay whole (one CTA per SM
+    // streams a chain as fast as two half chains).  TCASPMM_WINDOW_PARTS (clamped
+    // to [0, 64], 0 = this rule) sets the parts instead, at most one per stage.  A
+    // part of a consecutive column run starts 16 t0 columns in.
+    const int64_t nfb = (sh->ncols + MB - 1) / MB;
+    int64_t items = 0;
+    for (const Int4 &w : T.windows) items += w.x >= 0 ? 1 : (w.z + split - 1) / split;
+    items *= nfb;
+    const int auto_parts = items > 0 ? (int)std::min<int64_t>(64, std::max<int64_t>(1, nsm / items)) : 1;
+    const int env_parts = (int)env_int("TCASPMM_WINDOW_PARTS", 0, 0, 64);
     // TCASPMM_DENSE_RUNS=0 sends consecutive column runs through the gathered
     // path (tile indices, cp.async for 16-bit B) instead of TMA boxes.
     const bool dense_runs = env_flag("TCASPMM_DENSE_RUNS", true);
@@ -992,8 +1004,10 @@ tcaspmm_status tc_upload(const tcaspmm_csr &A, tcaspmm_dtype dt, Shard *sh)
     // windows 1.64 against 1.53 ms).
     const int32_t gathered = env_flag("TCASPMM_GATHER_TMA", true) ? -2 : -1;
     for (const Int4 &w : T.windows) {
-        const int parts = w.x >= 0 ? std::max(1, std::min(consec_parts, (w.z + Geo<0>::TPS - 1) / Geo<0>::TPS))
-                                   : (w.z + split - 1) / split;
+        const int stages = (w.z + Geo<0>::TPS - 1) / Geo<0>::TPS;
+        const int parts = w.x < 0       ? (w.z + split - 1) / split
+                          : env_parts > 0 ? std::max(1, std::min(env_parts, stages))
+                                          : std::max(1, std::min(auto_parts, stages / MIN_PART_STAGES));
         const int32_t run = w.x >= 0 && dense_runs ? dense_run(w) : -1;
         const int32_t dense = run >= 0 ? run : gathered;
         if (parts == 1) {
@@ -1062,7 +1076,6 @@ tcaspmm_status tc_upload(const tcaspmm_csr &A, tcaspmm_dtype dt, Shard *sh)
         }
     }
     sh->n_fallback = (int)fb.size();
-    const int64_t nfb = (sh->ncols + MB - 1) / MB;
     tcaspmm_status s;
     if ((s = upload_vec(sh, &sh->tc_tasks, td, "tc tasks")) != TCASPMM_OK) return s;
     if ((s = upload_vec(sh, &sh->tc_splits, ts, "tc splits")) != TCASPMM_OK) return s;

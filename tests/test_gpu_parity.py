@@ -206,6 +206,50 @@ def test_tensor_core_windows_mixed_with_residue():
     assert st["tc_windows"] == 16 and st["residue_nnz"] > 0
 
 
+@pytest.mark.parametrize("overlap", ["1", "0"])
+def test_mixed_plan_captured_in_a_cuda_graph(overlap, monkeypatch):
+    """A plan with tensor-core windows and residue rows forks its tensor-core kernel
+    onto a side stream and joins it back: captured in a CUDA graph on a non-default
+    stream and replayed, integer values bit-exact (and the same with both kernels on
+    the caller's stream)."""
+    monkeypatch.setenv("TCASPMM_OVERLAP", overlap)
+    g = np.random.default_rng(41)
+    A = _vstack(T.gen_uniform(512, 1024, 0.5, 3), T.gen_uniform(3000, 1024, 0.005, 4))
+    A = T.CSR(A.nrow, A.ncol, A.row_ptr, A.col, g.integers(-3, 4, A.nnz).astype(np.float32))
+    B = g.integers(-4, 5, (A.ncol, 128)).astype(np.float32)
+    Bd = torch.from_numpy(B).to(torch.float16).cuda()
+    Cd = torch.zeros((A.nrow, 128), dtype=torch.float32, device="cuda")
+    s = torch.cuda.Stream()
+    with T.Plan(A, 128, "f16") as p:
+        st = p.stats
+        assert st["tc_windows"] == 16 and st["residue_nnz"] > 0, st
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            p.execute1(Bd, Cd, stream=s)  # warm-up outside the capture
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            p.execute1(Bd, Cd, stream=s)
+        Cd.zero_()
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        p.sync_check()
+        del graph
+    np.testing.assert_array_equal(Cd.cpu().numpy(), reference(A, B, "f16").astype(np.float32))
+
+
+def test_few_windows_cut_into_parts_beside_the_residue():
+    """16 consecutive windows x 1 column block leave most of 148 SMs idle: their tile
+    chains are cut into parts and the tensor-core kernel runs beside the residue
+    kernel on the plan's side stream.  C1's 64 windows x 2 column blocks stay whole,
+    and with no residue rows nothing forks."""
+    A = _vstack(T.gen_uniform(512, 1024, 0.5, 3), T.gen_uniform(3000, 1024, 0.005, 4))
+    _, st = check(A, 128, "f16")
+    assert st["tc_windows"] == 16 and st["tc_tasks"] > 16 and st["tc_side_stream"] == 1, st
+    _, st = check(T.gen_uniform(2048, 512, 0.3, 0), 256, "f16")
+    assert st["tc_tasks"] == 64 and st["tc_side_stream"] == 0, st
+
+
 def test_tensor_core_partial_window_and_block():
     """M not a multiple of 32 rows, N not a multiple of 128 columns."""
     _, st = check(T.gen_uniform(1000, 300, 0.4, 11), 72, "f16")
