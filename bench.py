@@ -55,10 +55,11 @@ def load_peaks():
     return 6650.0, "fallback"
 
 
-def load_traffic(workload: str):
-    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary, or None."""
+def load_traffic(workload: str, profiled_config: bool = True):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary, or None
+    when there is none or this run is not the configuration that was profiled."""
     p = os.path.join(ROOT, "profiles", "traffic.json.txt")
-    if not os.path.exists(p):
+    if not profiled_config or not os.path.exists(p):
         return None
     with open(p) as f:
         d = json.load(f)
@@ -748,7 +749,10 @@ def main():
                        **({"epilogue": "C = relu(row_scale * (A B) + bias) stored as bf16"} if args.epilogue
                           else {})},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": load_traffic(args.workload),
+                         "frac": round(achieved / peak, 4),
+                         "traffic": load_traffic(args.workload, profiled_config=(
+                             dt == wl[3] and not args.epilogue and world == 1 and args.split == "columns"
+                             and not any(k.startswith("TCASPMM_") for k in os.environ))),
                          "peak_kind": peak_kind, "algorithmic_bytes": alg,
                          "kernel": "residue_kernel" if pst["tc_windows"] == 0 else "tc + residue"},
             "roofline_gather": {

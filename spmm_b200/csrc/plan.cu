@@ -158,7 +158,9 @@ tcaspmm_status build_shard(const tcaspmm_csr &Afull, tcaspmm_dtype dt, int devic
     // free, the tensor-core kernel runs on a side stream beside the residue rows
     // instead of before them (a few long tile chains no longer add their latency
     // to the residue kernel's); when they fill every slot, the two kernels would
-    // only contend, and run one after the other.  TCASPMM_OVERLAP=0 never forks.
+    // only contend (one tile CTA per SM beside the residue warps measured 1.71 ms on
+    // C3 with gathered windows, against 1.51 ms one after the other), and run one
+    // after the other.  TCASPMM_OVERLAP=0 never forks.
     const int64_t tc_units = (int64_t)sh->n_tasks * ((ncols + 127) / 128);
     if (sh->n_tasks > 0 && sh->n_ranges + sh->n_segs > 0 && tc_units < (int64_t)sh->tc_ctas_per_sm * sh->num_sms &&
         env_flag("TCASPMM_OVERLAP", true)) {
