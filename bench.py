@@ -362,6 +362,9 @@ def run_reference(args, wl):
     if args.dtype:
         dt = args.dtype
         desc += f" [dtype {dt}]"
+    if args.cols:
+        N = args.cols
+        desc += f" [N {N}]"
     T = HostGen()  # the same seeded inputs, without loading the GPU library
     A = build(T)
     B = T.gen_dense(A.ncol, N, 1, "f32")
@@ -424,6 +427,9 @@ def main():
                     help="1: bind each rank to its GPU's local CPUs (pinned buffers on that NUMA node)")
     ap.add_argument("--launch", default="graph", choices=["graph", "eager"],
                     help="timed step: replay a CUDA graph of the plan's launches, or call execute directly")
+    ap.add_argument("--cols", type=int, default=None,
+                    help="override the workload's N (e.g. --cols 16 on one GPU: the per-rank work of C3's "
+                         "8-GPU column split, for profiling)")
     ap.add_argument("--grid", default=None,
                     help="RxC shard grid for --split 2d (default: two column blocks when N GPUs is even)")
     args = ap.parse_args()
@@ -454,6 +460,9 @@ def main():
     if args.dtype:
         dt = args.dtype
         desc += f" [dtype {dt}]"
+    if args.cols:
+        N = args.cols
+        desc += f" [N {N}]"
     tdt = {"f32": torch.float32, "tf32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[dt]
     elem = 4 if dt in ("f32", "tf32") else 2
     A = build(T)
@@ -751,7 +760,8 @@ def main():
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4),
                          "traffic": load_traffic(args.workload, profiled_config=(
-                             dt == wl[3] and not args.epilogue and world == 1 and args.split == "columns"
+                             dt == wl[3] and N == wl[2] and not args.epilogue and world == 1
+                             and args.split == "columns"
                              and not any(k.startswith("TCASPMM_") for k in os.environ))),
                          "peak_kind": peak_kind, "algorithmic_bytes": alg,
                          "kernel": "residue_kernel" if pst["tc_windows"] == 0 else "tc + residue"},

@@ -62,3 +62,13 @@ def test_bf16_rounding_is_round_to_nearest_even():
     x = np.random.default_rng(0).standard_normal(10000).astype(np.float32)
     ref = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
     assert np.array_equal(bench._round_to(x, "bf16"), ref)
+
+
+def test_traffic_is_reported_only_for_the_profiled_configuration():
+    """The committed ncu DRAM bytes belong to one configuration per workload (its own
+    dtype and N, one GPU, column split, no tuning variables); any other run reports
+    traffic null rather than a figure measured on something else."""
+    assert bench.load_traffic("gcn") == bench.load_traffic("gcn", profiled_config=True)
+    assert isinstance(bench.load_traffic("gcn"), int) and bench.load_traffic("gcn") > 0
+    assert bench.load_traffic("gcn", profiled_config=False) is None
+    assert bench.load_traffic("no-such-workload") is None
