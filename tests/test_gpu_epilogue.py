@@ -145,3 +145,23 @@ def test_epilogue_through_gathered_windows(out, split, monkeypatch):
     monkeypatch.setenv("TCASPMM_SPLIT_TILES", split)
     st = _check(T.gen_rmat(15, 400000, kind="gcn", seed=2), 128, "f16", out, scale=_scale, bias=_bias, relu=True)
     assert st["tc_gathered_windows"] > 0
+
+
+@pytest.mark.parametrize("out", ["f32", "bf16"])
+def test_integer_epilogue_on_cut_chains_beside_the_residue(out):
+    """16 long consecutive windows (their tile chains cut into parts for the idle SMs and
+    reduced in part order) next to sparse rows on the residue kernel, the two kernels on
+    two streams: integers, power-of-two scales and an integer bias, bit-exact."""
+    rng = np.random.default_rng(17)
+    d, s = T.gen_uniform(512, 1024, 0.5, 3), T.gen_uniform(3000, 1024, 0.005, 4)
+    A = T.CSR(d.nrow + s.nrow, d.ncol, np.concatenate([d.row_ptr, s.row_ptr[1:] + d.nnz]),
+              np.concatenate([d.col, s.col]), None)
+    A = T.CSR(A.nrow, A.ncol, A.row_ptr, A.col, rng.integers(-3, 4, A.nnz).astype(np.float32))
+    B = np.round(T.gen_dense(1024, 128, 2, "f32") * 2).astype(np.float32)
+    scale = (2.0 ** rng.integers(-2, 2, A.nrow)).astype(np.float32)
+    bias = rng.integers(-3, 4, 128).astype(np.float32)
+    got, st = _run(A, B, "f16", scale=scale, bias=bias, relu=True, out=out)
+    assert st["tc_windows"] == 16 and st["tc_tasks"] > 16 and st["tc_side_stream"] == 1, st
+    ref = _reference(A, B, "f16", scale=scale, bias=bias, relu=True)
+    ref = torch.from_numpy(ref.astype(np.float32)).to(_TORCH[out]).float().numpy()
+    np.testing.assert_array_equal(got, ref)
