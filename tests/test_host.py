@@ -338,3 +338,24 @@ def test_gathered_windows_are_off_unless_asked_for(monkeypatch):
     assert np.all(cover == 1) and st["tc_gathered_windows"] == 0
     monkeypatch.setenv("TCASPMM_HUB_WINDOWS", "0")
     assert T.schedule_coverage(A, 128, "f16")[2]["tc_gathered_windows"] == 0
+
+
+def test_stats_struct_matches_the_header(tmp_path):
+    """The ctypes mirror of tcaspmm_plan_stats has the header's size and field offsets
+    (a field added on one side only would make the library write past the buffer)."""
+    import shutil
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    fields = [name for name, _ in T._Stats._fields_]
+    src = tmp_path / "stats.c"
+    src.write_text("#include <stdio.h>\n#include <stddef.h>\n#include \"tcaspmm.h\"\nint main(void) {\n"
+                   "  printf(\"%zu\\n\", sizeof(tcaspmm_plan_stats));\n"
+                   + "".join(f"  printf(\"%zu\\n\", offsetof(tcaspmm_plan_stats, {f}));\n" for f in fields)
+                   + "  return 0;\n}\n")
+    exe = tmp_path / "stats"
+    subprocess.run([cc, "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    out = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    assert out[0] == ctypes.sizeof(T._Stats)
+    assert out[1:] == [getattr(T._Stats, f).offset for f in fields]
