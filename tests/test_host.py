@@ -340,22 +340,26 @@ def test_gathered_windows_are_off_unless_asked_for(monkeypatch):
     assert T.schedule_coverage(A, 128, "f16")[2]["tc_gathered_windows"] == 0
 
 
-def test_stats_struct_matches_the_header(tmp_path):
-    """The ctypes mirror of tcaspmm_plan_stats has the header's size and field offsets
-    (a field added on one side only would make the library write past the buffer)."""
+@pytest.mark.parametrize("mirror,ctype", [("_Stats", "tcaspmm_plan_stats"), ("_CSR", "tcaspmm_csr"),
+                                           ("_RefCSR", "tcaspmm_ref_csr"), ("_Epilogue", "tcaspmm_epilogue")])
+def test_ctypes_structs_match_the_header(mirror, ctype, tmp_path):
+    """Each ctypes mirror of a header struct has the header's size and field offsets
+    (a field added on one side only would make the library read or write past the
+    caller's buffer)."""
     import shutil
 
     cc = shutil.which("gcc") or shutil.which("cc")
     if cc is None:
         pytest.skip("no C compiler")
-    fields = [name for name, _ in T._Stats._fields_]
-    src = tmp_path / "stats.c"
+    cls = getattr(T, mirror)
+    fields = [name for name, _ in cls._fields_]
+    src = tmp_path / "layout.c"
     src.write_text("#include <stdio.h>\n#include <stddef.h>\n#include \"tcaspmm.h\"\nint main(void) {\n"
-                   "  printf(\"%zu\\n\", sizeof(tcaspmm_plan_stats));\n"
-                   + "".join(f"  printf(\"%zu\\n\", offsetof(tcaspmm_plan_stats, {f}));\n" for f in fields)
+                   f"  printf(\"%zu\\n\", sizeof({ctype}));\n"
+                   + "".join(f"  printf(\"%zu\\n\", offsetof({ctype}, {f}));\n" for f in fields)
                    + "  return 0;\n}\n")
-    exe = tmp_path / "stats"
+    exe = tmp_path / "layout"
     subprocess.run([cc, "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
     out = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
-    assert out[0] == ctypes.sizeof(T._Stats)
-    assert out[1:] == [getattr(T._Stats, f).offset for f in fields]
+    assert out[0] == ctypes.sizeof(cls)
+    assert out[1:] == [getattr(cls, f).offset for f in fields]
