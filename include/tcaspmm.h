@@ -10,7 +10,12 @@
  *
  * Threading: a plan may be executed from one host thread on one stream at a
  * time (its scratch buffers are shared by all launches of that plan).
- * Different plans may run concurrently.
+ * Different plans may run concurrently.  A plan whose tensor-core windows
+ * leave SMs idle and that also has CUDA-core rows runs its tensor-core kernel
+ * on a side stream it owns, forked from the caller's stream and joined back to
+ * it by events inside each execute call (CUDA-graph capture sees two parallel
+ * kernel nodes); work ordered on the caller's stream before and after the
+ * call is ordered against both kernels.
  */
 #ifndef TCASPMM_H
 #define TCASPMM_H
