@@ -1,0 +1,51 @@
+"""Property test of the whole GPU path: random CSR matrices (empty rows, hub rows,
+dense row blocks that become tensor-core windows, K below a tile), random widths,
+dtypes and tuning variables -- gathered windows on or off, tile chains cut into
+parts or not, TMA gather4 or cp.async producers, the two kernels side by side or
+one after the other.  Values are small integers (A in [-3, 3], B in [-4, 4]), so
+every product and partial sum is exact in every input type and in fp32
+accumulation: the result must equal the fp64 oracle bit for bit.
+
+Examples are derandomized so every run checks the same cases."""
+import numpy as np
+import pytest
+import torch
+from hypothesis import given, settings
+from hypothesis import strategies as st
+
+import oracle
+import spmm_b200 as T
+from test_host_properties import _env, csr_cases
+
+pytestmark = pytest.mark.gpu
+
+_TORCH = {"f32": torch.float32, "tf32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+
+
+@settings(max_examples=200, deadline=None, derandomize=True)
+@given(A=csr_cases(),
+       N=st.sampled_from([1, 8, 16, 24, 64, 128, 136, 256]),
+       dt=st.sampled_from(["f32", "f16", "bf16", "tf32"]),
+       seed=st.integers(0, 2**31 - 1),
+       env=st.fixed_dictionaries({
+           "TCASPMM_HUB_WINDOWS": st.sampled_from([0, 1]),
+           "TCASPMM_TC_DENSITY": st.sampled_from([8, 32, 1024]),
+           "TCASPMM_WINDOW_PARTS": st.sampled_from([0, 1, 3]),
+           "TCASPMM_SPLIT_TILES": st.sampled_from([3, 128]),
+           "TCASPMM_GATHER_TMA": st.sampled_from([0, 1]),
+           "TCASPMM_OVERLAP": st.sampled_from([0, 1]),
+       }))
+def test_integer_products_are_exact_on_every_path(A, N, dt, seed, env):
+    rng = np.random.default_rng(seed)
+    A = T.CSR(A.nrow, A.ncol, A.row_ptr, A.col, rng.integers(-3, 4, A.nnz).astype(np.float32))
+    B = rng.integers(-4, 5, (A.ncol, N)).astype(np.float32)
+    Bd = torch.from_numpy(B).to(_TORCH[dt]).cuda()
+    Cd = torch.full((A.nrow, N), float("nan"), dtype=torch.float32, device="cuda")
+    with _env(env):
+        with T.Plan(A, N, dt) as p:
+            p.execute1(Bd, Cd, stream=torch.cuda.current_stream())
+            p.sync_check()
+            st_ = p.stats
+    torch.cuda.synchronize()
+    ref = oracle.spmm_f64(A.row_ptr, A.col, A.values().astype(np.float64), B.astype(np.float64))
+    np.testing.assert_array_equal(Cd.cpu().numpy(), ref.astype(np.float32), err_msg=str((env, st_)))
