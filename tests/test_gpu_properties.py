@@ -22,7 +22,7 @@ pytestmark = pytest.mark.gpu
 _TORCH = {"f32": torch.float32, "tf32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
 
 
-@settings(max_examples=200, deadline=None, derandomize=True)
+@settings(max_examples=400, deadline=None, derandomize=True)
 @given(A=csr_cases(),
        N=st.sampled_from([1, 8, 16, 24, 64, 128, 136, 256]),
        dt=st.sampled_from(["f32", "f16", "bf16", "tf32"]),
@@ -49,3 +49,34 @@ def test_integer_products_are_exact_on_every_path(A, N, dt, seed, env):
     torch.cuda.synchronize()
     ref = oracle.spmm_f64(A.row_ptr, A.col, A.values().astype(np.float64), B.astype(np.float64))
     np.testing.assert_array_equal(Cd.cpu().numpy(), ref.astype(np.float32), err_msg=str((env, st_)))
+
+
+@settings(max_examples=150, deadline=None, derandomize=True)
+@given(A=csr_cases(),
+       N=st.sampled_from([8, 16, 24, 64, 136, 256]),
+       dt=st.sampled_from(["f32", "f16", "tf32"]),
+       seed=st.integers(0, 2**31 - 1),
+       layout=st.sampled_from([("columns", 2, None), ("columns", 3, None), ("rows", 2, None), ("rows", 3, None),
+                               ("2d", 4, (2, 2)), ("2d", 2, (1, 2)), ("2d", 2, (2, 1))]))
+def test_shards_on_one_device_reassemble_the_exact_product(A, N, dt, seed, layout):
+    """Column, row and 2-D plans of 2-4 shards placed on cuda:0: every shard writes its
+    block of C (row block x column block) and together they give the oracle's product
+    bit for bit (integer values)."""
+    split, g, grid = layout
+    rng = np.random.default_rng(seed)
+    A = T.CSR(A.nrow, A.ncol, A.row_ptr, A.col, rng.integers(-3, 4, A.nnz).astype(np.float32))
+    B = rng.integers(-4, 5, (A.ncol, N)).astype(np.float32)
+    Bd = torch.from_numpy(B).to(_TORCH[dt]).cuda()
+    Cd = torch.full((A.nrow, N), float("nan"), dtype=torch.float32, device="cuda")
+    with T.Plan(A, N, dt, num_gpus=g, devices=[0] * g, split=split, grid=grid) as p:
+        blocks = []
+        for s in range(g):
+            r0, rc = p.shard_rows(s) if split != "columns" else (0, A.nrow)
+            c0, cc = p.shard(s)[1:] if split != "rows" else (0, N)
+            blocks.append((r0, rc, c0, cc))
+        p.execute([Bd[:, c0:c0 + cc] for _, _, c0, cc in blocks],
+                  [Cd[r0:r0 + rc, c0:c0 + cc] for r0, rc, c0, cc in blocks])
+        p.sync_check()
+    torch.cuda.synchronize()
+    ref = oracle.spmm_f64(A.row_ptr, A.col, A.values().astype(np.float64), B.astype(np.float64))
+    np.testing.assert_array_equal(Cd.cpu().numpy(), ref.astype(np.float32), err_msg=str((layout, blocks)))

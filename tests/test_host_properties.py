@@ -1,8 +1,9 @@
-"""Property tests of the host schedule (no GPU): for random CSR matrices -- empty
-rows, hub rows, dense row blocks that become tensor-core windows, K below a tile --
-random widths, dtypes and tuning variables, the schedule covers every nonzero
-exactly once, splits the nonzeros consistently between the tensor-core windows and
-the residue kernel, and never puts fp32 on the tensor cores.
+"""Property tests of the host schedule (no GPU): for random CSR matrices (empty
+rows, hub rows, dense row blocks that become tensor-core windows, some with tile
+chains of hundreds of tiles, K below a tile), random widths, dtypes and tuning
+variables, the schedule covers every nonzero exactly once, splits the nonzeros
+consistently between the tensor-core windows and the residue kernel, and never
+puts fp32 on the tensor cores.
 
 Examples are derandomized so every run checks the same cases."""
 import contextlib
@@ -31,19 +32,22 @@ def _env(values: dict):
 
 @st.composite
 def csr_cases(draw):
-    M = draw(st.integers(1, 400))
-    K = draw(st.integers(1, 600))
-    shape = draw(st.sampled_from(["sparse", "hubs", "dense_block", "empty_rows"]))
+    shape = draw(st.sampled_from(["sparse", "hubs", "dense_block", "empty_rows", "long_windows"]))
+    M = draw(st.integers(1, 400 if shape != "long_windows" else 160))
+    K = draw(st.integers(1, 600) if shape != "long_windows" else st.integers(600, 6000))
     rng = np.random.default_rng(draw(st.integers(0, 2**31 - 1)))
-    lam = {"sparse": 3.0, "hubs": 2.0, "dense_block": 1.0, "empty_rows": 0.3}[shape]
+    lam = {"sparse": 3.0, "hubs": 2.0, "dense_block": 1.0, "empty_rows": 0.3, "long_windows": 2.0}[shape]
     lens = np.minimum(rng.poisson(lam, M), K)
     if shape == "hubs":
         for r in rng.choice(M, size=min(M, 4), replace=False):
             lens[r] = rng.integers(K // 2, K + 1)
-    if shape == "dense_block":
+    if shape in ("dense_block", "long_windows"):
+        # A block of rows dense enough for tensor-core windows; with long_windows
+        # their tile chains run to hundreds of tiles (many index chunks and parts).
+        lo, hi = (0.2, 0.9) if shape == "dense_block" else (0.05, 0.4)
         r0 = int(rng.integers(0, M))
         rows = np.arange(r0, min(M, r0 + int(rng.integers(16, 97))))
-        lens[rows] = np.maximum(1, (K * rng.uniform(0.2, 0.9, rows.size)).astype(np.int64))
+        lens[rows] = np.maximum(1, (K * rng.uniform(lo, hi, rows.size)).astype(np.int64))
     cols = [np.sort(rng.choice(K, size=int(n), replace=False)).astype(np.int32) for n in lens]
     rp = np.zeros(M + 1, np.int64)
     rp[1:] = np.cumsum(lens)
