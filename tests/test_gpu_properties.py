@@ -80,3 +80,30 @@ def test_shards_on_one_device_reassemble_the_exact_product(A, N, dt, seed, layou
     torch.cuda.synchronize()
     ref = oracle.spmm_f64(A.row_ptr, A.col, A.values().astype(np.float64), B.astype(np.float64))
     np.testing.assert_array_equal(Cd.cpu().numpy(), ref.astype(np.float32), err_msg=str((layout, blocks)))
+
+
+@settings(max_examples=80, deadline=None, derandomize=True)
+@given(A=csr_cases(),
+       N=st.sampled_from([1, 8, 16, 64, 128]),
+       dt=st.sampled_from([torch.float32, torch.float16, torch.bfloat16]),
+       seed=st.integers(0, 2**31 - 1))
+def test_torch_op_forward_and_backward_are_exact(A, N, dt, seed):
+    """torch.ops.tcaspmm.spmm on random graphs with integer values: Y = A X (fp32) and,
+    through autograd, dX = A^T dY (returned in X's dtype), both equal to the fp64
+    oracle bit for bit after that one rounding (the op's plan cache sees a new graph
+    every example)."""
+    from spmm_b200 import torch_op  # registers the op
+
+    rng = np.random.default_rng(seed)
+    val = rng.integers(-3, 4, A.nnz).astype(np.float32)
+    crow, col, vt = torch.from_numpy(A.row_ptr), torch.from_numpy(A.col), torch.from_numpy(val)
+    X = torch.from_numpy(rng.integers(-4, 5, (A.ncol, N)).astype(np.float32)).to(dt).cuda().requires_grad_(True)
+    Y = torch.ops.tcaspmm.spmm(crow, col, vt, X)
+    ref = oracle.spmm_f64(A.row_ptr, A.col, val.astype(np.float64), X.detach().double().cpu().numpy())
+    np.testing.assert_array_equal(Y.detach().float().cpu().numpy(), ref.astype(np.float32))
+    G = torch.from_numpy(rng.integers(-2, 3, (A.nrow, N)).astype(np.float32)).cuda().to(Y.dtype)
+    (Y * G).sum().backward()
+    At = torch_op._host_csr(crow, col, vt, A.ncol, transposed=True)
+    gref = oracle.spmm_f64(At.row_ptr, At.col, At.values().astype(np.float64), G.double().cpu().numpy())
+    gref = torch.from_numpy(gref.astype(np.float32)).to(dt).float().numpy()
+    np.testing.assert_array_equal(X.grad.float().cpu().numpy(), gref)
