@@ -107,3 +107,41 @@ def test_torch_op_forward_and_backward_are_exact(A, N, dt, seed):
     gref = oracle.spmm_f64(At.row_ptr, At.col, At.values().astype(np.float64), G.double().cpu().numpy())
     gref = torch.from_numpy(gref.astype(np.float32)).to(dt).float().numpy()
     np.testing.assert_array_equal(X.grad.float().cpu().numpy(), gref)
+
+
+_OUT_T = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+
+
+@settings(max_examples=120, deadline=None, derandomize=True)
+@given(A=csr_cases(),
+       N=st.sampled_from([8, 16, 64, 128, 136]),
+       dt=st.sampled_from(["f32", "f16", "bf16", "tf32"]),
+       out=st.sampled_from(["f32", "f16", "bf16"]),
+       terms=st.fixed_dictionaries({"scale": st.booleans(), "bias": st.booleans(), "relu": st.booleans()}),
+       seed=st.integers(0, 2**31 - 1))
+def test_fused_epilogue_is_exact_up_to_the_output_rounding(A, N, dt, out, terms, seed):
+    """relu?(row_scale * (A B) + bias) in one launch, on every kernel path: with integer
+    values, power-of-two row scales and an integer bias every step is exact in fp32,
+    so C equals the fp64 oracle rounded once to the output type."""
+    rng = np.random.default_rng(seed)
+    A = T.CSR(A.nrow, A.ncol, A.row_ptr, A.col, rng.integers(-3, 4, A.nnz).astype(np.float32))
+    B = rng.integers(-4, 5, (A.ncol, N)).astype(np.float32)
+    scale = (2.0 ** rng.integers(-2, 2, A.nrow)).astype(np.float32) if terms["scale"] else None
+    bias = rng.integers(-3, 4, N).astype(np.float32) if terms["bias"] else None
+    Bd = torch.from_numpy(B).to(_TORCH[dt]).cuda()
+    Cd = torch.full((A.nrow, N), float("nan"), dtype=_OUT_T[out], device="cuda")
+    ep = T.Epilogue(torch.from_numpy(scale).cuda() if scale is not None else None,
+                    torch.from_numpy(bias).cuda() if bias is not None else None, terms["relu"], out)
+    with T.Plan(A, N, dt) as p:
+        p.execute1(Bd, Cd, stream=torch.cuda.current_stream(), epilogue=ep)
+        p.sync_check()
+    torch.cuda.synchronize()
+    ref = oracle.spmm_f64(A.row_ptr, A.col, A.values().astype(np.float64), B.astype(np.float64))
+    if scale is not None:
+        ref = ref * scale.astype(np.float64)[:, None]
+    if bias is not None:
+        ref = ref + bias.astype(np.float64)[None, :]
+    if terms["relu"]:
+        ref = np.maximum(ref, 0.0)
+    ref = torch.from_numpy(ref.astype(np.float32)).to(_OUT_T[out]).float().numpy()
+    np.testing.assert_array_equal(Cd.float().cpu().numpy(), ref)
