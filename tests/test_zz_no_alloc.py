@@ -15,9 +15,12 @@ import ctypes as C
 
 import numpy as np
 import pytest
+from hypothesis import given, settings
+from hypothesis import strategies as st
 
 import oracle
 import spmm_b200 as T
+from test_host_properties import csr_cases
 
 _fn = T.lib.tcaspmm_spmm_csr_noalloc
 _fn.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_void_p, C.c_int64,
@@ -99,3 +102,30 @@ def test_noalloc_matches_plan_entry_on_two_calls(case, dt, N):
     # The first call may commit the library's device image (lazy loading); after it,
     # a call must leave the device's free memory exactly where it was.
     assert free[1] == free[0], f"device free memory moved by {free[0] - free[1]} bytes on the second call"
+
+
+
+@pytest.mark.gpu
+@settings(max_examples=120, deadline=None, derandomize=True)
+@given(A=csr_cases(), N=st.sampled_from([1, 4, 8, 16, 64, 136, 256]),
+       dt=st.sampled_from(["f32", "f16", "bf16"]), seed=st.integers(0, 2**31 - 1))
+def test_noalloc_is_exact_on_random_integer_matrices(A, N, dt, seed):
+    """Random matrices (empty rows, hub rows, dense blocks, K below a tile) with small
+    integer values through the no-allocation entry point: exact against the fp64
+    oracle in every input type."""
+    import torch
+
+    tdt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[dt]
+    rng = np.random.default_rng(seed)
+    vals = rng.integers(-3, 4, A.nnz).astype(np.float32)
+    Bh = rng.integers(-4, 5, (A.ncol, N)).astype(np.float32)
+    dev = torch.device("cuda", 0)
+    B = torch.from_numpy(Bh).to(tdt).to(dev)
+    rp = torch.from_numpy(A.row_ptr.astype(np.int32)).to(dev)
+    col = torch.from_numpy(A.col).to(dev)
+    val = torch.from_numpy(vals).to(tdt).to(dev)
+    out = torch.full((A.nrow, N), float("nan"), device=dev)
+    _noalloc(rp, col, val, A.nrow, A.ncol, A.nnz, B, out, dt, torch.cuda.current_stream(dev))
+    torch.cuda.synchronize(dev)
+    exact = oracle.spmm_f64(A.row_ptr, A.col, vals.astype(np.float64), Bh.astype(np.float64))
+    np.testing.assert_array_equal(out.cpu().numpy(), exact.astype(np.float32))
