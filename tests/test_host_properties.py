@@ -3,13 +3,15 @@ rows, hub rows, dense row blocks that become tensor-core windows, some with tile
 chains of hundreds of tiles, K below a tile), random widths, dtypes and tuning
 variables, the schedule covers every nonzero exactly once, splits the nonzeros
 consistently between the tensor-core windows and the residue kernel, and never
-puts fp32 on the tensor cores.
+puts fp32 on the tensor cores; one corruption of such a matrix is refused at the
+boundary.
 
 Examples are derandomized so every run checks the same cases."""
 import contextlib
 import os
 
 import numpy as np
+import pytest
 from hypothesis import given, settings
 from hypothesis import strategies as st
 
@@ -77,3 +79,42 @@ def test_schedule_covers_every_nonzero_once(A, N, dt, env):
         assert s["tc_windows"] == 0
     if env["TCASPMM_HUB_WINDOWS"] == 0:
         assert s["tc_gathered_windows"] == 0
+
+
+@settings(max_examples=200, deadline=None, derandomize=True)
+@given(A=csr_cases(), how=st.sampled_from(["col_high", "col_negative", "duplicate", "unsorted",
+                                           "ptr_decreases", "ptr_end", "ptr_start"]),
+       pick=st.integers(0, 2**31 - 1))
+def test_malformed_csr_is_rejected_not_computed(A, how, pick):
+    """One corruption of a valid CSR -- a column out of range or negative, a repeated
+    or out-of-order column in a row, row offsets that decrease or do not span nnz --
+    is refused at the boundary with a format error (never a crash, never a product
+    that silently mis-sums a repeated column on the tensor cores)."""
+    T.schedule_coverage(A, 16, "f16")  # the valid matrix passes
+    rp, col = A.row_ptr.copy(), A.col.copy()
+    multi = np.flatnonzero(np.diff(rp) >= 2)  # rows with two or more nonzeros
+    rng = np.random.default_rng(pick)
+    if how == "col_high" and A.nnz:
+        col[rng.integers(A.nnz)] = A.ncol
+    elif how == "col_negative" and A.nnz:
+        col[rng.integers(A.nnz)] = -1
+    elif how in ("duplicate", "unsorted") and multi.size:
+        r = multi[rng.integers(multi.size)]
+        j = rp[r] + rng.integers(rp[r + 1] - rp[r] - 1)
+        if how == "duplicate":
+            col[j + 1] = col[j]
+        else:
+            col[j], col[j + 1] = col[j + 1], col[j]
+    elif how == "ptr_decreases" and A.nrow >= 2 and A.nnz:
+        i = 1 + rng.integers(A.nrow - 1)
+        rp[i] = rp[i + 1] + 1 if rp[i + 1] + 1 <= A.nnz else rp[i - 1] - 1
+    elif how == "ptr_end":
+        rp[-1] = A.nnz + 1
+    elif how == "ptr_start":
+        rp[0] = 1
+    else:
+        return  # this matrix has nothing to corrupt that way
+    bad = T.CSR(A.nrow, A.ncol, rp, col, A.values())
+    with pytest.raises(T.TcaspmmError) as e:
+        T.schedule_coverage(bad, 16, "f16")
+    assert e.value.status in (T.Status.FORMAT, T.Status.INVALID_ARG), e.value
