@@ -118,3 +118,19 @@ def test_malformed_csr_is_rejected_not_computed(A, how, pick):
     with pytest.raises(T.TcaspmmError) as e:
         T.schedule_coverage(bad, 16, "f16")
     assert e.value.status in (T.Status.FORMAT, T.Status.INVALID_ARG), e.value
+
+
+@settings(max_examples=80, deadline=None, derandomize=True)
+@given(A=csr_cases(), pattern=st.booleans())
+def test_matrix_files_round_trip(A, pattern, tmp_path_factory):
+    """A random matrix written as .smtx (with its .val values, or as a pattern) and as
+    binary CSR reads back identical: offsets, columns and values bit for bit."""
+    d = tmp_path_factory.mktemp("files")
+    M = T.CSR(A.nrow, A.ncol, A.row_ptr, A.col, None if pattern else A.values())
+    T.smtx_write(str(d / "a.smtx"), M)
+    T.csrbin_write(str(d / "a.csrb"), M)
+    for back in (T.smtx_read(str(d / "a.smtx")), T.csrbin_read(str(d / "a.csrb"))):
+        assert (back.nrow, back.ncol, back.nnz) == (M.nrow, M.ncol, M.nnz)
+        np.testing.assert_array_equal(back.row_ptr, M.row_ptr)
+        np.testing.assert_array_equal(back.col, M.col)
+        np.testing.assert_array_equal(back.values(), M.values())
