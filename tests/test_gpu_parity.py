@@ -167,23 +167,39 @@ def test_reference_entry_point_bit_exact(bundled):
     np.testing.assert_array_equal(Cout.reshape(M, N), bundled["C_int"])
 
 
-def test_multi_gpu_column_shards():
+@pytest.mark.parametrize("case", ["gcn_f32", "mixed_f16"])
+def test_multi_gpu_column_shards(case):
+    """One plan over two GPUs, each owning a column block of B and C.  mixed_f16:
+    tensor-core windows beside residue rows, so each device's shard runs its tile
+    kernel on its own side stream; integer values, bit-exact."""
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("one GPU")
-    A = T.gen_rmat(14, 100000, kind="gcn", seed=1)
-    N, dt = 128, "f32"
-    B = T.gen_dense(A.ncol, N, 3, "f32")
+    if case == "gcn_f32":
+        A = T.gen_rmat(14, 100000, kind="gcn", seed=1)
+        N, dt = 128, "f32"
+        B = T.gen_dense(A.ncol, N, 3, "f32")
+    else:
+        g = np.random.default_rng(43)
+        A = _vstack(T.gen_uniform(512, 1024, 0.5, 3), T.gen_uniform(3000, 1024, 0.005, 4))
+        A = T.CSR(A.nrow, A.ncol, A.row_ptr, A.col, g.integers(-3, 4, A.nnz).astype(np.float32))
+        N, dt = 256, "f16"
+        B = g.integers(-4, 5, (A.ncol, N)).astype(np.float32)
     with T.Plan(A, N, dt, num_gpus=2) as p:
         Bs, Cs = [], []
         for s in range(2):
             dev, b, c = p.shard(s)
-            Bs.append(torch.from_numpy(B[:, b:b + c].copy()).to(f"cuda:{dev}"))
+            Bs.append(torch.from_numpy(B[:, b:b + c].copy()).to(_torch_dt(dt)).to(f"cuda:{dev}"))
             Cs.append(torch.empty((A.nrow, c), device=f"cuda:{dev}"))
         p.execute(Bs, Cs, streams=[torch.cuda.current_stream(f"cuda:{p.shard(s)[0]}") for s in range(2)])
         p.sync_check()
+        st = p.stats
         out = np.hstack([c.cpu().numpy() for c in Cs])
-    assert oracle.rel_l2(out, reference(A, B, dt)) <= TOL_CORE
+    if case == "gcn_f32":
+        assert oracle.rel_l2(out, reference(A, B, dt)) <= TOL_CORE
+    else:
+        assert st["tc_windows"] == 16 and st["tc_side_stream"] == 1, st
+        np.testing.assert_array_equal(out, reference(A, B, dt).astype(np.float32))
 
 
 @pytest.mark.parametrize("dt", ["f16", "bf16", "tf32"])
