@@ -996,7 +996,7 @@ tcaspmm_status tc_upload(const tcaspmm_csr &A, tcaspmm_dtype dt, Shard *sh)
     const int auto_parts = items > 0 ? (int)std::min<int64_t>(64, std::max<int64_t>(1, nsm / items)) : 1;
     const int env_parts = (int)env_int("TCASPMM_WINDOW_PARTS", 0, 0, 64);
     // TCASPMM_DENSE_RUNS=0 sends consecutive column runs through the gathered
-    // path (tile indices, cp.async for 16-bit B) instead of TMA boxes.
+    // path (tile indices and the gathered-tile producer) instead of TMA boxes.
     const bool dense_runs = env_flag("TCASPMM_DENSE_RUNS", true);
     // Gathered 16-bit tiles are fetched by TMA gather4 (as TF32 tiles are);
     // TCASPMM_GATHER_TMA=0 fetches them by cp.async from all producer threads
